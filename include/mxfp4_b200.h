@@ -1,0 +1,158 @@
+/*
+ * mxfp4_b200.h -- C ABI of libmxfp4_b200.so, the B200 (sm_100a) MXFP4 backend.
+ *
+ * This is the drop-in boundary for the operator surface of
+ * lutianshu824/mxfp4-gfx936 (file "src/aiter/ops/triton/moe_op_mxfp4_soft.py",
+ * cited below as soft:LINE, and the vLLM adapter
+ * "integration/vllm/vllm_mxfp4_gfx936.py", cited as vllm:LINE).  The Python
+ * operator module binds these symbols with ctypes; any other FFI can bind them
+ * the same way.
+ *
+ * Conventions shared by every entry point:
+ *  - All tensor arguments are device pointers owned by the caller; the library
+ *    allocates no memory on the compute path.  Scratch space is passed as
+ *    `workspace` and sized by the matching *_workspace_size() query.
+ *  - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
+ *    legacy default stream) and runs asynchronously; no entry point
+ *    synchronises the host on the compute path.
+ *  - Matrices are row-major with an explicit leading dimension in ELEMENTS
+ *    (bytes for uint8 tensors).  Packed MXFP4 holds two E2M1 codes per byte,
+ *    the low nibble is the even K index; E8M0 scales are uint8, one per 32
+ *    values along K, row-major [rows, K/32] (the swizzled AITER scale layout is
+ *    rejected, soft:398-399).
+ *  - Return value: MXFP4_OK or an MXFP4_ERR_* code; mxfp4_last_error() gives a
+ *    message for the calling thread.  Nothing aborts or prints.
+ */
+#ifndef MXFP4_B200_H_
+#define MXFP4_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MXFP4_B200_ABI_VERSION 1
+
+/* status codes */
+#define MXFP4_OK 0
+#define MXFP4_ERR_INVALID_ARGUMENT 1   /* bad shape, stride, alignment or null pointer */
+#define MXFP4_ERR_UNSUPPORTED_DEVICE 2 /* not an sm_100 device */
+#define MXFP4_ERR_CUDA 3               /* a CUDA runtime / driver call failed */
+#define MXFP4_ERR_TIMEOUT 4            /* a device-side bounded wait expired */
+#define MXFP4_ERR_WORKSPACE 5          /* workspace missing or too small */
+#define MXFP4_ERR_UNSUPPORTED 6        /* valid request this backend does not implement */
+
+/* element types */
+#define MXFP4_DTYPE_F32 0
+#define MXFP4_DTYPE_BF16 1
+#define MXFP4_DTYPE_F16 2
+#define MXFP4_DTYPE_U8 3
+#define MXFP4_DTYPE_I32 4
+#define MXFP4_DTYPE_I64 5
+
+/* dense W4A16 execution modes (explicit backend selection, soft:45-49) */
+#define MXFP4_LINEAR_FUSED 0 /* decode inside the GEMM producer (replaces soft:176-274) */
+#define MXFP4_LINEAR_SAFE 1  /* explicit dequant into workspace, then the same GEMM (soft:371-373) */
+
+/* Library ABI version (MXFP4_B200_ABI_VERSION). */
+int mxfp4_abi_version(void);
+
+/* Message for the last failing call made by this thread ("" if none). */
+const char* mxfp4_last_error(void);
+
+/* 1 if `device` is an sm_100 GPU this library can run on, else 0. */
+int mxfp4_device_supported(int device);
+
+/* Device status word written by kernels (MXFP4_OK or the first error code a
+ * kernel recorded, e.g. MXFP4_ERR_TIMEOUT).  Synchronises `device`.  With
+ * clear != 0 the word is reset to MXFP4_OK afterwards. */
+int mxfp4_device_status(int device, int clear);
+
+/* ------------------------------------------------------------------------ */
+/* K0 -- dequantisation.  Replaces dequant_mxfp4 (soft:277-307).            */
+/* out[r, k] = E2M1[code(r,k)] * 2^(scale(r, k/32) - 127), computed in FP32  */
+/* and rounded to out_dtype (F32, BF16 or F16); scale code 255 gives NaN.    */
+/* packed: [rows, k/2] u8 contiguous; scales: [rows, k/32] u8 contiguous;    */
+/* out: [rows, k] contiguous.  k % 32 == 0.                                 */
+int mxfp4_dequant(const void* packed, const void* scales, void* out, int out_dtype, int64_t rows,
+                  int64_t k, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* K1 -- dense W4A16 linear.  Replaces linear_mxfp4_soft (soft:310-376),     */
+/* including its Triton kernel (soft:176-274).                               */
+/* out[m, n] = round(sum_k x[m,k] * W[n,k]) (+ bias[n], rounded again), with */
+/* W = dequant(w_packed, w_scales) in x's dtype, FP32 accumulation in one    */
+/* reduction per output.  x_dtype: BF16 or F16; out has x's dtype; bias is   */
+/* NULL or a [n] vector of x's dtype.  k % 128 == 0.  ldx/ldo in elements,   */
+/* ldw/lds in bytes (>= k/2, >= k/32).                                       */
+size_t mxfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int x_dtype, int mode);
+int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw,
+                       const void* w_scales, int64_t lds, const void* bias, void* out, int64_t ldo,
+                       int64_t m, int64_t n, int64_t k, int mode, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* K4 -- device routing.  Replaces _make_routing (vllm:119-146) without its  */
+/* host sync.  Route r = t*top_k + j of topk_ids[num_tokens, top_k] (I32 or  */
+/* I64) goes to local expert e = id - expert_offset when 0 <= e <           */
+/* num_experts, else it is dropped.  Output: sorted_ids [capacity] (route   */
+/* ids grouped by expert in ascending expert order, ascending route id      */
+/* inside an expert, each expert padded to a multiple of block_m with the    */
+/* value num_tokens*top_k), block_expert [capacity/block_m] (expert of each  */
+/* block, -1 after the last used block) and num_post_padded [1] (used       */
+/* length).  capacity = mxfp4_moe_route_capacity(...).                       */
+int64_t mxfp4_moe_route_capacity(int64_t num_routes, int num_experts, int block_m);
+size_t mxfp4_moe_route_workspace_size(int64_t num_routes, int num_experts);
+int mxfp4_moe_route(const void* topk_ids, int ids_dtype, int64_t num_tokens, int top_k,
+                    int num_experts, int expert_offset, int block_m, int32_t* sorted_ids,
+                    int32_t* block_expert, int32_t* num_post_padded, int64_t capacity,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* K3 -- routed MoE op.  Replaces fused_moe_mxfp4_soft (soft:379-494) and     */
+/* its Triton kernel (soft:65-173).                                          */
+/* C[t, j, :] = round(round(round(A'[t] . W[e]^T) * a_scale) * b_scale[e])    */
+/* (then * topk_weights[t, j] and rounded again if mul_routed_weight) for    */
+/* e = topk_ids[t, j] in [0, num_experts); other routes leave C[t, j, :] = 0.*/
+/* A' = A in C's dtype, or dequant(A, a_mx_scale) when a_dtype is U8 (W4A4,  */
+/* soft:468-475).  Rounding is to c_dtype (F32, BF16 or F16).                */
+/* A: [num_tokens, k] (a_dtype BF16/F16/F32, or U8 packed [num_tokens, k/2]  */
+/* with a_mx_scale [num_tokens, k/32]); B: [num_experts, n, k/2] u8;         */
+/* B_mx: [num_experts, n, k/32] u8; a_scale: 1 FP32; b_scale: [num_experts]  */
+/* FP32; topk_weights: [num_tokens, top_k] (w_dtype F32/BF16/F16); topk_ids: */
+/* [num_tokens, top_k] I32/I64; C: [num_tokens, top_k, n] contiguous.        */
+/* All contiguous; k % 128 == 0.                                             */
+size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t n,
+                                      int64_t k, int a_dtype, int c_dtype);
+int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const void* B,
+                    const void* B_mx_scale, const float* a_scale, const float* b_scale,
+                    const void* topk_weights, int w_dtype, const void* topk_ids, int ids_dtype,
+                    void* C, int c_dtype, int64_t num_tokens, int top_k, int num_experts,
+                    int64_t n, int64_t k, int mul_routed_weight, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* K3+K5 -- MoE layer.  Replaces _moe_apply (vllm:233-265) with the W4A16    */
+/* MXFP4 experts: gate_up = x . W13[e]^T (gate = first `inter` rows), h =    */
+/* bf16(bf16(silu(gate)) * up), y_r = bf16(bf16(h . W2[e]^T) * w_r) per      */
+/* route, out[t] = bf16(sum_j y_(t*top_k+j)) with FP32 accumulation.        */
+/* x: [num_tokens, hidden] BF16; w13: [E, 2*inter, hidden/2] u8 + scales    */
+/* [E, 2*inter, hidden/32]; w2: [E, hidden, inter/2] u8 + scales            */
+/* [E, hidden, inter/32]; topk_weights F32/BF16/F16 and topk_ids I32/I64     */
+/* [num_tokens, top_k]; out: [num_tokens, hidden] BF16.  hidden % 128 == 0, */
+/* inter % 128 == 0.                                                        */
+size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts,
+                                      int64_t hidden, int64_t inter);
+int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const void* w2,
+                    const void* w2_scale, const void* topk_weights, int w_dtype,
+                    const void* topk_ids, int ids_dtype, void* out, int64_t num_tokens,
+                    int top_k, int num_experts, int64_t hidden, int64_t inter, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXFP4_B200_H_ */

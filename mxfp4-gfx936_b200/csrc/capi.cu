@@ -1,0 +1,617 @@
+// Host side of libmxfp4_b200.so: argument validation, tensor-map encoding,
+// workspace layout and kernel launches behind the C ABI in include/mxfp4_b200.h.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "elementwise.cuh"
+#include "gemm.cuh"
+
+using namespace mx;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+#define MX_CUDA(call)                                                                      \
+  do {                                                                                     \
+    cudaError_t e_ = (call);                                                               \
+    if (e_ != cudaSuccess)                                                                 \
+      return fail(MXFP4_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));     \
+  } while (0)
+
+#define MX_CHECK(cond, msg)                                                                \
+  do {                                                                                     \
+    if (!(cond)) return fail(MXFP4_ERR_INVALID_ARGUMENT, msg);                             \
+  } while (0)
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// --- device properties -----------------------------------------------------
+struct DevInfo {
+  int sms = 0;
+  int major = 0, minor = 0;
+  bool ok = false;
+};
+
+int current_device_info(DevInfo& info) {
+  static std::mutex mu;
+  static DevInfo cache[64];
+  int dev = 0;
+  MX_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(MXFP4_ERR_UNSUPPORTED_DEVICE, "device index out of range");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cache[dev].ok) {
+    cudaDeviceProp prop;
+    MX_CUDA(cudaGetDeviceProperties(&prop, dev));
+    cache[dev].sms = prop.multiProcessorCount;
+    cache[dev].major = prop.major;
+    cache[dev].minor = prop.minor;
+    cache[dev].ok = true;
+  }
+  info = cache[dev];
+  if (info.major != 10)
+    return fail(MXFP4_ERR_UNSUPPORTED_DEVICE,
+                "libmxfp4_b200 needs an sm_100 (B200) device, found sm_" +
+                    std::to_string(info.major) + std::to_string(info.minor));
+  return MXFP4_OK;
+}
+
+// --- tensor maps -----------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encoder(EncodeTiledFn& fn) {
+  static EncodeTiledFn cached = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) cached = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (cached == nullptr)
+    return fail(MXFP4_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  fn = cached;
+  return MXFP4_OK;
+}
+
+// 2-D row-major tensor [rows, cols] of `esize`-byte elements, row pitch in bytes.
+int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int esize,
+                uint64_t cols, uint64_t rows, uint64_t pitch_bytes, uint32_t box_cols,
+                uint32_t box_rows, CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc;
+  if (int rc = get_encoder(enc)) return rc;
+  if (!aligned(base, 16)) return fail(MXFP4_ERR_INVALID_ARGUMENT, "TMA operand must be 16-byte aligned");
+  if (pitch_bytes % 16 != 0)
+    return fail(MXFP4_ERR_INVALID_ARGUMENT, "TMA operand row pitch must be a multiple of 16 bytes");
+  (void)esize;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MXFP4_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+  return MXFP4_OK;
+}
+
+int elem_size(int dtype) {
+  switch (dtype) {
+    case MXFP4_DTYPE_F32: return 4;
+    case MXFP4_DTYPE_BF16: return 2;
+    case MXFP4_DTYPE_F16: return 2;
+    case MXFP4_DTYPE_U8: return 1;
+    case MXFP4_DTYPE_I32: return 4;
+    case MXFP4_DTYPE_I64: return 8;
+  }
+  return 0;
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// --- GEMM launch ------------------------------------------------------------
+template <int AMODE, int BMODE, int EPI, bool FP16>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+                cudaStream_t stream) {
+  using Cfg = GemmCfg<BMODE>;
+  auto kern = mxfp4_gemm_kernel<AMODE, BMODE, EPI, FP16>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  });
+  MX_CUDA(attr_err);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+int check_scales_layout(int64_t k) {
+  if (k <= 0 || k % 128 != 0)
+    return fail(MXFP4_ERR_INVALID_ARGUMENT, "logical K must be a positive multiple of 128, got " + std::to_string(k));
+  return MXFP4_OK;
+}
+
+// --- routing ----------------------------------------------------------------
+struct RouteWs {
+  int32_t* rank;
+  int32_t* hist;
+  int32_t* blk_off;
+};
+
+size_t route_ws_bytes(int64_t num_routes, int num_experts) {
+  const int64_t chunks = (num_routes + kRouteThreads - 1) / kRouteThreads;
+  return align_up(sizeof(int32_t) * std::max<int64_t>(num_routes, 1), 256) +
+         align_up(sizeof(int32_t) * std::max<int64_t>(chunks, 1) * num_experts, 256) +
+         align_up(sizeof(int32_t) * num_experts, 256);
+}
+
+RouteWs carve_route_ws(uint8_t* ws, int64_t num_routes, int num_experts) {
+  const int64_t chunks = (num_routes + kRouteThreads - 1) / kRouteThreads;
+  RouteWs r;
+  r.rank = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * std::max<int64_t>(num_routes, 1), 256);
+  r.hist = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * std::max<int64_t>(chunks, 1) * num_experts, 256);
+  r.blk_off = reinterpret_cast<int32_t*>(ws);
+  return r;
+}
+
+int64_t route_capacity(int64_t num_routes, int num_experts, int block_m) {
+  const int64_t padded = num_routes + static_cast<int64_t>(num_experts) * (block_m - 1);
+  return (padded + block_m - 1) / block_m * block_m;
+}
+
+int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_experts,
+              int expert_offset, int block_m, int32_t* sorted_ids, int32_t* block_expert,
+              int32_t* post, int64_t capacity, uint8_t* ws, cudaStream_t stream) {
+  RouteWs r = carve_route_ws(ws, num_routes, num_experts);
+  const int64_t chunks = std::max<int64_t>((num_routes + kRouteThreads - 1) / kRouteThreads, 1);
+  const size_t smem = sizeof(int32_t) * kRouteWarps * num_experts;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(route_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    sizeof(int32_t) * kRouteWarps * kMaxExperts);
+  });
+  MX_CUDA(attr_err);
+  if (num_routes > 0)
+    route_count_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, smem, stream>>>(
+        ids, ids_dtype, num_routes, num_experts, expert_offset, r.rank, r.hist);
+  else
+    MX_CUDA(cudaMemsetAsync(r.hist, 0, sizeof(int32_t) * num_experts, stream));
+  MX_CUDA(cudaGetLastError());
+  route_offsets_kernel<<<1, 1024, 0, stream>>>(r.hist, static_cast<int>(chunks), num_experts, block_m,
+                                               num_routes, r.blk_off, sorted_ids, block_expert, post,
+                                               capacity / block_m);
+  MX_CUDA(cudaGetLastError());
+  if (num_routes > 0)
+    route_scatter_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, 0, stream>>>(
+        ids, ids_dtype, num_routes, num_experts, expert_offset, block_m, r.rank, r.hist, r.blk_off,
+        sorted_ids);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+// Launch a grouped GEMM over routed blocks (block size kBM).
+template <int AMODE, int EPI>
+int grouped_gemm(bool fp16, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                 int sms, cudaStream_t stream) {
+  const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms)));
+  if (fp16) return launch_gemm<AMODE, B_DECODE, EPI, true>(ta, tb, p, grid, stream);
+  return launch_gemm<AMODE, B_DECODE, EPI, false>(ta, tb, p, grid, stream);
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int mxfp4_abi_version(void) { return MXFP4_B200_ABI_VERSION; }
+
+const char* mxfp4_last_error(void) { return t_last_error.c_str(); }
+
+int mxfp4_device_supported(int device) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return prop.major == 10 ? 1 : 0;
+}
+
+int mxfp4_device_status(int device, int clear) {
+  int prev = 0;
+  MX_CUDA(cudaGetDevice(&prev));
+  MX_CUDA(cudaSetDevice(device));
+  MX_CUDA(cudaDeviceSynchronize());
+  int word = 0;
+  MX_CUDA(cudaMemcpyFromSymbol(&word, g_status, sizeof(int)));
+  if (clear) {
+    const int zero = 0;
+    MX_CUDA(cudaMemcpyToSymbol(g_status, &zero, sizeof(int)));
+  }
+  MX_CUDA(cudaSetDevice(prev));
+  return word;
+}
+
+int mxfp4_dequant(const void* packed, const void* scales, void* out, int out_dtype, int64_t rows,
+                  int64_t k, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(packed && scales && out, "null pointer");
+  MX_CHECK(rows >= 0 && k >= 0 && k % 32 == 0, "logical K must be divisible by 32");
+  MX_CHECK(out_dtype == MXFP4_DTYPE_F32 || out_dtype == MXFP4_DTYPE_BF16 || out_dtype == MXFP4_DTYPE_F16,
+           "dequant output dtype must be F32, BF16 or F16");
+  MX_CHECK(aligned(packed, 16) && aligned(out, 16), "packed and out must be 16-byte aligned");
+  const int64_t nb = rows * (k / 32);
+  if (nb == 0) return MXFP4_OK;
+  const int grid = static_cast<int>(std::min<int64_t>((nb + 255) / 256, int64_t(info.sms) * 8));
+  cudaStream_t s = as_stream(stream);
+  if (out_dtype == MXFP4_DTYPE_BF16)
+    dequant_kernel<MXFP4_DTYPE_BF16><<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(packed),
+                                                          static_cast<const uint8_t*>(scales), out, nb);
+  else if (out_dtype == MXFP4_DTYPE_F16)
+    dequant_kernel<MXFP4_DTYPE_F16><<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(packed),
+                                                         static_cast<const uint8_t*>(scales), out, nb);
+  else
+    dequant_kernel<MXFP4_DTYPE_F32><<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(packed),
+                                                         static_cast<const uint8_t*>(scales), out, nb);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+size_t mxfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int x_dtype, int mode) {
+  (void)m;
+  (void)x_dtype;
+  if (mode != MXFP4_LINEAR_SAFE) return 0;
+  return align_up(static_cast<size_t>(n) * k * 2, 256);
+}
+
+int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw,
+                       const void* w_scales, int64_t lds, const void* bias, void* out, int64_t ldo,
+                       int64_t m, int64_t n, int64_t k, int mode, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(x && w_packed && w_scales && out, "null pointer");
+  MX_CHECK(x_dtype == MXFP4_DTYPE_BF16 || x_dtype == MXFP4_DTYPE_F16, "x must be BF16 or F16");
+  MX_CHECK(mode == MXFP4_LINEAR_FUSED || mode == MXFP4_LINEAR_SAFE, "unknown linear mode");
+  if (int rc = check_scales_layout(k)) return rc;
+  MX_CHECK(m >= 0 && n > 0, "bad M/N");
+  MX_CHECK(m < (int64_t(1) << 31) && n < (int64_t(1) << 31) && k < (int64_t(1) << 30), "dimension too large");
+  MX_CHECK(ldx >= k && ldo >= n && ldw >= k / 2 && lds >= k / 32, "leading dimension too small");
+  MX_CHECK(aligned(w_scales, 4) && lds % 4 == 0, "scales must be 4-byte aligned rows");
+  if (m == 0) return MXFP4_OK;
+  cudaStream_t s = as_stream(stream);
+  const bool fp16 = x_dtype == MXFP4_DTYPE_F16;
+  const CUtensorMapDataType xt = fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+
+  CUtensorMap ta, tb;
+  if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+
+  GemmParams p{};
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.num_m_blocks = static_cast<int>((m + kBM - 1) / kBM);
+  p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
+  p.w_scales = static_cast<const uint8_t*>(w_scales);
+  p.lds = lds;
+  p.w_rows_per_expert = n;
+  p.out = out;
+  p.ldo = ldo;
+  p.out_dtype = x_dtype;
+  p.bias = bias;
+  p.vec_ok = aligned(out, 16) && (ldo * 2) % 16 == 0;
+  const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, info.sms));
+
+  if (mode == MXFP4_LINEAR_FUSED) {
+    if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kBK / 2,
+                             kBN / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    if (fp16) return launch_gemm<A_TMA, B_DECODE, EPI_DENSE, true>(ta, tb, p, grid, s);
+    return launch_gemm<A_TMA, B_DECODE, EPI_DENSE, false>(ta, tb, p, grid, s);
+  }
+  // safe: explicit dequant of W into the workspace, then the same MMA pipeline
+  const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
+  MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
+  if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
+  if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (fp16) return launch_gemm<A_TMA, B_TMA, EPI_DENSE, true>(ta, tb, p, grid, s);
+  return launch_gemm<A_TMA, B_TMA, EPI_DENSE, false>(ta, tb, p, grid, s);
+}
+
+int64_t mxfp4_moe_route_capacity(int64_t num_routes, int num_experts, int block_m) {
+  if (num_routes < 0 || num_experts <= 0 || block_m <= 0) return 0;
+  return route_capacity(num_routes, num_experts, block_m);
+}
+
+size_t mxfp4_moe_route_workspace_size(int64_t num_routes, int num_experts) {
+  return route_ws_bytes(num_routes, num_experts);
+}
+
+int mxfp4_moe_route(const void* topk_ids, int ids_dtype, int64_t num_tokens, int top_k,
+                    int num_experts, int expert_offset, int block_m, int32_t* sorted_ids,
+                    int32_t* block_expert, int32_t* num_post_padded, int64_t capacity,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(ids_dtype == MXFP4_DTYPE_I32 || ids_dtype == MXFP4_DTYPE_I64, "topk_ids must be I32 or I64");
+  MX_CHECK(num_tokens >= 0 && top_k > 0, "bad num_tokens/top_k");
+  MX_CHECK(num_experts > 0 && num_experts <= kMaxExperts, "num_experts must be in [1, 1024]");
+  MX_CHECK(block_m > 0 && block_m <= 4096, "bad block_m");
+  const int64_t routes = num_tokens * top_k;
+  MX_CHECK(routes < (int64_t(1) << 31), "too many routes");
+  MX_CHECK(sorted_ids && block_expert && num_post_padded && (routes == 0 || topk_ids), "null pointer");
+  MX_CHECK(capacity >= route_capacity(routes, num_experts, block_m) && capacity % block_m == 0,
+           "capacity smaller than mxfp4_moe_route_capacity()");
+  if (workspace == nullptr || workspace_bytes < route_ws_bytes(routes, num_experts))
+    return fail(MXFP4_ERR_WORKSPACE, "routing workspace too small");
+  return run_route(topk_ids, ids_dtype, routes, num_experts, expert_offset, block_m, sorted_ids,
+                   block_expert, num_post_padded, capacity, static_cast<uint8_t*>(workspace),
+                   as_stream(stream));
+}
+
+// Workspace of the routed op: routing arrays, routing scratch, converted A.
+size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t n,
+                                      int64_t k, int a_dtype, int c_dtype) {
+  (void)n;
+  const int64_t routes = num_tokens * top_k;
+  const int64_t cap = route_capacity(routes, num_experts, kBM);
+  size_t b = 0;
+  b += align_up(sizeof(int32_t) * cap, 256);
+  b += align_up(sizeof(int32_t) * (cap / kBM + 1), 256);
+  b += 256;  // num_post_padded
+  b += route_ws_bytes(routes, num_experts);
+  const int cdt = c_dtype == MXFP4_DTYPE_F32 ? a_dtype : c_dtype;
+  if (a_dtype != cdt || a_dtype == MXFP4_DTYPE_U8) b += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
+  return b;
+}
+
+int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const void* B,
+                    const void* B_mx_scale, const float* a_scale, const float* b_scale,
+                    const void* topk_weights, int w_dtype, const void* topk_ids, int ids_dtype,
+                    void* C, int c_dtype, int64_t num_tokens, int top_k, int num_experts,
+                    int64_t n, int64_t k, int mul_routed_weight, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  if (int rc = check_scales_layout(k)) return rc;
+  MX_CHECK(A && B && B_mx_scale && a_scale && b_scale && topk_ids && C, "null pointer");
+  MX_CHECK(c_dtype == MXFP4_DTYPE_F32 || c_dtype == MXFP4_DTYPE_BF16 || c_dtype == MXFP4_DTYPE_F16,
+           "C must be F32, BF16 or F16");
+  MX_CHECK(a_dtype == MXFP4_DTYPE_U8 || a_dtype == MXFP4_DTYPE_BF16 || a_dtype == MXFP4_DTYPE_F16 ||
+               a_dtype == MXFP4_DTYPE_F32,
+           "A must be U8 (packed MXFP4), BF16, F16 or F32");
+  MX_CHECK(a_dtype != MXFP4_DTYPE_U8 || a_mx_scale != nullptr, "packed MXFP4 activations require A_mx_scale");
+  MX_CHECK(!mul_routed_weight || topk_weights != nullptr, "route weights required");
+  MX_CHECK(w_dtype == MXFP4_DTYPE_F32 || w_dtype == MXFP4_DTYPE_BF16 || w_dtype == MXFP4_DTYPE_F16,
+           "topk_weights must be F32, BF16 or F16");
+  MX_CHECK(num_tokens >= 0 && top_k > 0 && num_experts > 0 && num_experts <= kMaxExperts && n > 0,
+           "bad sizes");
+  MX_CHECK(num_tokens * top_k < (int64_t(1) << 31) && n < (int64_t(1) << 31), "dimension too large");
+  // the compute dtype of the MMA: C's dtype, or A's 16-bit dtype when C is F32
+  int cdt = c_dtype;
+  if (c_dtype == MXFP4_DTYPE_F32) {
+    if (a_dtype == MXFP4_DTYPE_F32)
+      return fail(MXFP4_ERR_UNSUPPORTED, "F32 activations with an F32 output are not supported by the B200 backend");
+    cdt = a_dtype == MXFP4_DTYPE_U8 ? MXFP4_DTYPE_BF16 : a_dtype;
+  }
+  const size_t need = mxfp4_fused_moe_workspace_size(num_tokens, top_k, num_experts, n, k, a_dtype, c_dtype);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(MXFP4_ERR_WORKSPACE, "fused MoE needs " + std::to_string(need) + " workspace bytes");
+  cudaStream_t s = as_stream(stream);
+  const int64_t routes = num_tokens * top_k;
+  const int esz = elem_size(c_dtype);
+  if (routes == 0) return MXFP4_OK;
+  // C.zero_() (soft:476): routes to other experts stay zero
+  MX_CUDA(cudaMemsetAsync(C, 0, static_cast<size_t>(routes) * n * esz, s));
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int64_t cap = route_capacity(routes, num_experts, kBM);
+  int32_t* sorted_ids = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * cap, 256);
+  int32_t* block_expert = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * (cap / kBM + 1), 256);
+  int32_t* post = reinterpret_cast<int32_t*>(ws);
+  ws += 256;
+  uint8_t* route_ws = ws;
+  ws += route_ws_bytes(routes, num_experts);
+  const void* a_eff = A;
+  if (a_dtype == MXFP4_DTYPE_U8) {
+    if (int rc = mxfp4_dequant(A, a_mx_scale, ws, cdt, num_tokens, k, stream)) return rc;
+    a_eff = ws;
+  } else if (a_dtype != cdt) {
+    const int64_t cnt = num_tokens * k;
+    const int grid = static_cast<int>(std::min<int64_t>((cnt + 255) / 256, int64_t(info.sms) * 8));
+    cast_kernel<<<grid, 256, 0, s>>>(A, a_dtype, ws, cdt, cnt);
+    MX_CUDA(cudaGetLastError());
+    a_eff = ws;
+  }
+  if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kBM, sorted_ids, block_expert, post,
+                         cap, route_ws, s))
+    return rc;
+
+  CUtensorMap ta{}, tb;
+  if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, static_cast<uint64_t>(num_experts) * n,
+                           k / 2, kBK / 2, kBN / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
+  GemmParams p{};
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.num_m_blocks = static_cast<int>(cap / kBM);
+  p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
+  p.a_ptr = static_cast<const uint8_t*>(a_eff);
+  p.lda = k;
+  p.a_rows = static_cast<int>(num_tokens);
+  p.w_scales = static_cast<const uint8_t*>(B_mx_scale);
+  p.lds = k / 32;
+  p.w_rows_per_expert = n;
+  p.sorted_ids = sorted_ids;
+  p.block_expert = block_expert;
+  p.num_post_padded = post;
+  p.num_routes = static_cast<int>(routes);
+  p.top_k = top_k;
+  p.out = C;
+  p.out_dtype = c_dtype;
+  p.a_scale = a_scale;
+  p.b_scale = b_scale;
+  p.topk_w = topk_weights;
+  p.w_dtype = w_dtype;
+  p.mul_w = mul_routed_weight ? 1 : 0;
+  p.c_stride_t = static_cast<int64_t>(top_k) * n;
+  p.c_stride_j = n;
+  p.vec_ok = aligned(C, 16) && (n * esz) % 16 == 0;
+  return grouped_gemm<A_GATHER, EPI_MOE>(cdt == MXFP4_DTYPE_F16, ta, tb, p, info.sms, s);
+}
+
+size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t hidden,
+                                      int64_t inter) {
+  const int64_t routes = num_tokens * top_k;
+  const int64_t cap = route_capacity(routes, num_experts, kBM);
+  size_t b = 0;
+  b += align_up(sizeof(int32_t) * cap, 256);
+  b += align_up(sizeof(int32_t) * (cap / kBM + 1), 256);
+  b += 256;
+  b += route_ws_bytes(routes, num_experts);
+  b += align_up(static_cast<size_t>(cap) * inter * 2, 256);     // h in routed order
+  b += align_up(static_cast<size_t>(routes) * hidden * 2, 256); // weighted down rows
+  return b;
+}
+
+int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const void* w2,
+                    const void* w2_scale, const void* topk_weights, int w_dtype,
+                    const void* topk_ids, int ids_dtype, void* out, int64_t num_tokens, int top_k,
+                    int num_experts, int64_t hidden, int64_t inter, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(x && w13 && w13_scale && w2 && w2_scale && topk_weights && topk_ids && out, "null pointer");
+  MX_CHECK(hidden > 0 && hidden % 128 == 0, "hidden must be a positive multiple of 128");
+  MX_CHECK(inter > 0 && inter % 128 == 0, "intermediate size must be a positive multiple of 128");
+  MX_CHECK(num_tokens >= 0 && top_k > 0 && num_experts > 0 && num_experts <= kMaxExperts, "bad sizes");
+  MX_CHECK(w_dtype == MXFP4_DTYPE_F32 || w_dtype == MXFP4_DTYPE_BF16 || w_dtype == MXFP4_DTYPE_F16,
+           "topk_weights must be F32, BF16 or F16");
+  MX_CHECK(ids_dtype == MXFP4_DTYPE_I32 || ids_dtype == MXFP4_DTYPE_I64, "topk_ids must be I32 or I64");
+  MX_CHECK(aligned(x, 16) && aligned(out, 16), "x and out must be 16-byte aligned");
+  const size_t need = mxfp4_moe_layer_workspace_size(num_tokens, top_k, num_experts, hidden, inter);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(MXFP4_ERR_WORKSPACE, "MoE layer needs " + std::to_string(need) + " workspace bytes");
+  cudaStream_t s = as_stream(stream);
+  const int64_t routes = num_tokens * top_k;
+  if (num_tokens == 0) return MXFP4_OK;
+  const int64_t cap = route_capacity(routes, num_experts, kBM);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* sorted_ids = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * cap, 256);
+  int32_t* block_expert = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * (cap / kBM + 1), 256);
+  int32_t* post = reinterpret_cast<int32_t*>(ws);
+  ws += 256;
+  uint8_t* route_ws = ws;
+  ws += route_ws_bytes(routes, num_experts);
+  void* hbuf = ws;
+  ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
+  void* ybuf = ws;
+
+  if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kBM, sorted_ids, block_expert, post, cap,
+                         route_ws, s))
+    return rc;
+
+  // gate_up with fused SiLU(gate) * up -> h [cap, inter] in routed order
+  {
+    CUtensorMap ta{}, tb;
+    if (int rc = make_map_2d(&tb, w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hidden / 2,
+                             static_cast<uint64_t>(num_experts) * 2 * inter, hidden / 2, kBK / 2, kBN / 2,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    GemmParams p{};
+    p.N = static_cast<int>(2 * inter);
+    p.K = static_cast<int>(hidden);
+    p.num_m_blocks = static_cast<int>(cap / kBM);
+    p.num_n_blocks = static_cast<int>((inter + kBN / 2 - 1) / (kBN / 2));
+    p.a_ptr = static_cast<const uint8_t*>(x);
+    p.lda = hidden;
+    p.a_rows = static_cast<int>(num_tokens);
+    p.w_scales = static_cast<const uint8_t*>(w13_scale);
+    p.lds = hidden / 32;
+    p.w_rows_per_expert = 2 * inter;
+    p.glu_inter = static_cast<int>(inter);
+    p.sorted_ids = sorted_ids;
+    p.block_expert = block_expert;
+    p.num_post_padded = post;
+    p.num_routes = static_cast<int>(routes);
+    p.top_k = top_k;
+    p.out = hbuf;
+    p.ldo = inter;
+    p.out_dtype = MXFP4_DTYPE_BF16;
+    p.vec_ok = 1;
+    if (int rc = grouped_gemm<A_GATHER, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
+  }
+  // down with route weights, scattered to y[route] = [routes, hidden]
+  {
+    CUtensorMap ta, tb;
+    if (int rc = make_map_2d(&ta, hbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inter, cap, inter * 2, kBK, kBM,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = make_map_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inter / 2,
+                             static_cast<uint64_t>(num_experts) * hidden, inter / 2, kBK / 2, kBN / 2,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    GemmParams p{};
+    p.N = static_cast<int>(hidden);
+    p.K = static_cast<int>(inter);
+    p.num_m_blocks = static_cast<int>(cap / kBM);
+    p.num_n_blocks = static_cast<int>((hidden + kBN - 1) / kBN);
+    p.w_scales = static_cast<const uint8_t*>(w2_scale);
+    p.lds = inter / 32;
+    p.w_rows_per_expert = hidden;
+    p.sorted_ids = sorted_ids;
+    p.block_expert = block_expert;
+    p.num_post_padded = post;
+    p.num_routes = static_cast<int>(routes);
+    p.top_k = 1;
+    p.out = ybuf;
+    p.out_dtype = MXFP4_DTYPE_BF16;
+    p.a_scale = nullptr;
+    p.b_scale = nullptr;
+    p.topk_w = topk_weights;
+    p.w_dtype = w_dtype;
+    p.mul_w = 1;
+    p.c_stride_t = hidden;
+    p.c_stride_j = 0;
+    p.vec_ok = 1;
+    if (int rc = grouped_gemm<A_TMA, EPI_MOE>(false, ta, tb, p, info.sms, s)) return rc;
+  }
+  const int64_t vecs = num_tokens * (hidden / 8);
+  const int grid = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, int64_t(info.sms) * 8));
+  combine_topk_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(ybuf),
+                                           static_cast<__nv_bfloat16*>(out), num_tokens, top_k, hidden);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+}  // extern "C"

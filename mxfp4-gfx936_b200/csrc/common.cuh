@@ -1,0 +1,351 @@
+// Device-side building blocks for the sm_100a MXFP4 kernels: shared-memory
+// mbarriers with bounded waits, TMA tile loads, cp.async row gathers, the
+// tcgen05 (UMMA) instruction family and the E2M1 -> BF16/FP16 decoder.
+//
+// Every wait in this library is bounded: a wait that exceeds kWaitCycles
+// records MXFP4_ERR_TIMEOUT in the library's device status word, raises the
+// CTA-local abort flag and returns false, so that the kernel can drain its
+// in-flight asynchronous work, free its tensor memory and exit normally.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/mxfp4_b200.h"
+
+namespace mx {
+
+// ~2 s at the B200 boost clock; no legitimate wait in these kernels is longer
+// than a few microseconds.
+constexpr long long kWaitCycles = 4000000000LL;
+
+// Device status word: 0 = ok, otherwise the first MXFP4_ERR_* code a kernel
+// recorded.  Read and cleared by mxfp4_device_status().  The library is one
+// translation unit (capi.cu includes every kernel header), so this is the
+// only definition.
+__device__ int g_status = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void record_error(int code) { atomicCAS(&g_status, 0, code); }
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait until the phase with the given parity has completed.  Returns false
+// when the CTA is aborting (another role timed out) or this wait timed out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort_flag = 1;
+      record_error(MXFP4_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA and cp.async
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                            int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+// Same, with an L2 cache-policy hint (createpolicy result).
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                 int x, int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// 16-byte global -> shared copy; src_bytes == 0 zero-fills the destination.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+// Arrive on `bar` once all earlier cp.async of this thread have landed; the
+// arrival is pre-counted in the barrier's expected count.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+// Make this thread's generic-proxy shared-memory accesses visible to the async
+// proxy (TMA, tcgen05.mma).
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 / tensor memory
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {  // whole warp
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (BF16 or FP16 inputs, FP32 accumulate).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Block-scaled FP4 x FP4 with UE8M0 scale factors (one per 32 K) read from TMEM.
+__device__ __forceinline__ void umma_mxf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// Arrive on `bar` when all earlier tcgen05 async operations of this thread complete.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// Copy 4 x 32 lanes x 128 bit of scale factors from shared memory (described by
+// a no-swizzle matrix descriptor) into TMEM, replicated into all four lane quarters.
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored in the
+// 128-byte swizzle layout (rows of 128 bytes, 8-row groups 1024 bytes apart).
+// Bits: [0,14) start>>4, [16,30) LBO>>4, [32,46) SBO>>4, [46,48) version=1,
+// [61,64) layout (2 = 128B swizzle).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>(1) << 16;            // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;    // SBO: next 8-row group
+  d |= static_cast<uint64_t>(1) << 46;            // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: FP32 accumulator, K-major A and B.
+// in_fmt: 0 = FP16, 1 = BF16.  Bits: [4,6) c fmt, [7,10) a fmt, [10,13) b fmt,
+// [17,23) N>>3, [24,29) M>>4.
+__host__ __device__ constexpr uint32_t idesc_f16(int in_fmt, int m, int n) {
+  return (1u << 4) | (static_cast<uint32_t>(in_fmt) << 7) | (static_cast<uint32_t>(in_fmt) << 10) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// E2M1 decode
+// ---------------------------------------------------------------------------
+// Byte tables for the eight E2M1 magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6} as
+// BF16: low bytes {00,00,80,C0,00,40,80,C0}, high bytes {00,3F,3F,3F,40,40,40,40}.
+constexpr uint32_t kLoTab0 = 0xC0800000u, kLoTab1 = 0xC0804000u;
+constexpr uint32_t kHiTab0 = 0x3F3F3F00u, kHiTab1 = 0x40404040u;
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// Eight E2M1 codes (one 32-bit word, element j in nibble j, i.e. low nibble of
+// each byte = even K) -> eight unscaled BF16 values in K order, as 4 words.
+__device__ __forceinline__ void e2m1x8_to_bf16x8(uint32_t w, uint32_t (&o)[4]) {
+  const uint32_t mag = w & 0x77777777u;
+  const uint32_t mag_hi = mag >> 16;
+  const uint32_t lo03 = prmt(kLoTab0, kLoTab1, mag);
+  const uint32_t lo47 = prmt(kLoTab0, kLoTab1, mag_hi);
+  uint32_t hi03 = prmt(kHiTab0, kHiTab1, mag);
+  uint32_t hi47 = prmt(kHiTab0, kHiTab1, mag_hi);
+  const uint32_t s_even = (w << 4) & 0x80808080u;  // byte j: sign of element 2j
+  const uint32_t s_odd = w & 0x80808080u;          // byte j: sign of element 2j+1
+  hi03 |= prmt(s_even, s_odd, 0x5140u);
+  hi47 |= prmt(s_even, s_odd, 0x7362u);
+  o[0] = prmt(lo03, hi03, 0x5140u);
+  o[1] = prmt(lo03, hi03, 0x7362u);
+  o[2] = prmt(lo47, hi47, 0x5140u);
+  o[3] = prmt(lo47, hi47, 0x7362u);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// E8M0 code -> BF16 bits of 2^(code-127): code 0 is the subnormal 2^-127 and
+// code 255 is NaN.  Replicated into both halves of a bf16x2 word.
+__device__ __forceinline__ uint32_t e8m0_to_bf16x2(uint32_t code) {
+  uint32_t b = code == 0 ? 0x0040u : (code == 255 ? 0x7FC0u : (code << 7));
+  return b | (b << 16);
+}
+// E8M0 code -> FP32 2^(code-127) (code 0 subnormal, 255 NaN).
+__device__ __forceinline__ float e8m0_to_f32(uint32_t code) {
+  uint32_t b = code == 0 ? 0x00400000u : (code == 255 ? 0x7FC00000u : (code << 23));
+  return __uint_as_float(b);
+}
+
+// Eight codes -> eight BF16 values scaled by 2^(code-127), exactly as
+// bf16(fp32(value) * fp32(scale)): every such product is representable in
+// BF16 (or overflows to inf in both), so one bf16x2 multiply per pair is exact.
+__device__ __forceinline__ uint4 decode8_bf16(uint32_t w, uint32_t scale_bf16x2) {
+  uint32_t o[4];
+  e2m1x8_to_bf16x8(w, o);
+  return make_uint4(bf16x2_mul(o[0], scale_bf16x2), bf16x2_mul(o[1], scale_bf16x2),
+                    bf16x2_mul(o[2], scale_bf16x2), bf16x2_mul(o[3], scale_bf16x2));
+}
+
+__device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// Eight codes -> eight FP16 values: FP32 product, then round to FP16.
+__device__ __forceinline__ uint4 decode8_f16(uint32_t w, float scale) {
+  uint32_t o[4];
+  e2m1x8_to_bf16x8(w, o);
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(o[i] << 16) * scale;
+    const float hi = __uint_as_float(o[i] & 0xFFFF0000u) * scale;
+    r[i] = f32x2_to_f16x2(lo, hi);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_nc_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// Rounding helpers for the output dtypes.
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+__device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ float round_to(float x, int dtype) {
+  return dtype == MXFP4_DTYPE_BF16 ? round_bf16(x) : (dtype == MXFP4_DTYPE_F16 ? round_f16(x) : x);
+}
+
+}  // namespace mx

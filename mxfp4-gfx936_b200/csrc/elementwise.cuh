@@ -1,0 +1,210 @@
+// Bandwidth-bound kernels of the MXFP4 path:
+//   K0  dequant        packed E2M1 + E8M0 -> F32 / BF16 / F16 (dequant_mxfp4, soft:277-307)
+//   K4  routing        stable per-expert padded blocks (_make_routing, vllm:119-146)
+//   K5  combine        sum over top-k routed rows (vllm:263-265)
+//   --  cast           activation dtype conversion for the routed op (soft:473-475)
+#pragma once
+
+#include "common.cuh"
+
+namespace mx {
+
+// ---------------------------------------------------------------------------
+// K0: one thread per 32-element block (16 packed bytes + 1 scale byte).
+// ---------------------------------------------------------------------------
+template <int OUT>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ packed,
+                                                      const uint8_t* __restrict__ scales,
+                                                      void* __restrict__ out, int64_t num_blocks) {
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < num_blocks;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 q = *reinterpret_cast<const uint4*>(packed + b * 16);
+    const uint32_t code = scales[b];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    if (OUT == MXFP4_DTYPE_BF16) {
+      const uint32_t sc = e8m0_to_bf16x2(code);
+      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + b * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = decode8_bf16(w[i], sc);
+    } else if (OUT == MXFP4_DTYPE_F16) {
+      const float sc = e8m0_to_f32(code);
+      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + b * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = decode8_f16(w[i], sc);
+    } else {
+      const float sc = e8m0_to_f32(code);
+      float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + b * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t v[4];
+        e2m1x8_to_bf16x8(w[i], v);
+        o[2 * i] = make_float4(__uint_as_float(v[0] << 16) * sc, __uint_as_float(v[0] & 0xFFFF0000u) * sc,
+                               __uint_as_float(v[1] << 16) * sc, __uint_as_float(v[1] & 0xFFFF0000u) * sc);
+        o[2 * i + 1] = make_float4(__uint_as_float(v[2] << 16) * sc, __uint_as_float(v[2] & 0xFFFF0000u) * sc,
+                                   __uint_as_float(v[3] << 16) * sc, __uint_as_float(v[3] & 0xFFFF0000u) * sc);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// activation cast (A.to(C.dtype), soft:475): src dtype -> dst dtype, rounding.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) cast_kernel(const void* __restrict__ src, int src_dtype,
+                                                   void* __restrict__ dst, int dst_dtype, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v;
+    if (src_dtype == MXFP4_DTYPE_F32) v = static_cast<const float*>(src)[i];
+    else if (src_dtype == MXFP4_DTYPE_BF16) v = __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i]);
+    else v = __half2float(static_cast<const __half*>(src)[i]);
+    if (dst_dtype == MXFP4_DTYPE_BF16) static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
+    else if (dst_dtype == MXFP4_DTYPE_F16) static_cast<__half*>(dst)[i] = __float2half_rn(v);
+    else static_cast<float*>(dst)[i] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K4 routing, three passes over the routes (stable counting sort):
+//   pass 1 (route_count): each CTA takes a contiguous chunk of routes, ranks
+//          every route among the earlier routes of the same expert in its
+//          chunk (warp __match_any_sync + per-warp counts) and writes the
+//          chunk histogram;
+//   pass 2 (route_offsets): one CTA turns the [chunks x experts] histogram
+//          into per-chunk bases, pads every expert to block_m, writes the
+//          per-block expert ids, the pad entries and the used length;
+//   pass 3 (route_scatter): every route lands at block_offset(e) + chunk
+//          base + rank.
+// No host synchronisation; everything stays on the stream.
+// ---------------------------------------------------------------------------
+constexpr int kRouteThreads = 512;
+constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr int kMaxExperts = 1024;
+
+__device__ __forceinline__ int load_expert(const void* ids, int ids_dtype, int64_t r) {
+  return ids_dtype == MXFP4_DTYPE_I64 ? static_cast<int>(static_cast<const int64_t*>(ids)[r])
+                                      : static_cast<const int32_t*>(ids)[r];
+}
+
+// smem: warp_cnt[kRouteWarps][E] ints.  rank_out[r] = rank in chunk; hist[c][e].
+__global__ void __launch_bounds__(kRouteThreads) route_count_kernel(
+    const void* __restrict__ ids, int ids_dtype, int64_t num_routes, int num_experts,
+    int expert_offset, int32_t* __restrict__ rank_out, int32_t* __restrict__ hist) {
+  extern __shared__ int32_t warp_cnt[];  // [kRouteWarps][num_experts]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kRouteWarps * num_experts; i += blockDim.x) warp_cnt[i] = 0;
+  __syncthreads();
+  const int64_t r = blockIdx.x * static_cast<int64_t>(kRouteThreads) + threadIdx.x;
+  int e = -1;
+  if (r < num_routes) {
+    e = load_expert(ids, ids_dtype, r) - expert_offset;
+    if (e < 0 || e >= num_experts) e = -1;
+  }
+  const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+  const int rank_in_warp = __popc(peers & ((1u << lane) - 1u));
+  if (e >= 0 && rank_in_warp == 0) warp_cnt[warp * num_experts + e] = __popc(peers);
+  __syncthreads();
+  // exclusive prefix over warps, per expert; chunk histogram
+  for (int x = threadIdx.x; x < num_experts; x += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kRouteWarps; ++w) {
+      const int c = warp_cnt[w * num_experts + x];
+      warp_cnt[w * num_experts + x] = run;
+      run += c;
+    }
+    hist[static_cast<int64_t>(blockIdx.x) * num_experts + x] = run;
+  }
+  __syncthreads();
+  if (r < num_routes) rank_out[r] = e >= 0 ? warp_cnt[warp * num_experts + e] + rank_in_warp : -1;
+}
+
+// One CTA.  hist[c][e] -> chunk bases (in place); blk_off[e] = first block of e.
+__global__ void __launch_bounds__(1024) route_offsets_kernel(
+    int32_t* __restrict__ hist, int num_chunks, int num_experts, int block_m, int64_t num_routes,
+    int32_t* __restrict__ blk_off, int32_t* __restrict__ sorted_ids,
+    int32_t* __restrict__ block_expert, int32_t* __restrict__ num_post_padded,
+    int64_t capacity_blocks) {
+  __shared__ int32_t nblk[kMaxExperts];
+  __shared__ int32_t scan[kMaxExperts];
+  __shared__ int32_t total_s[kMaxExperts];
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
+    int run = 0;
+    for (int c = 0; c < num_chunks; ++c) {
+      const int64_t i = static_cast<int64_t>(c) * num_experts + e;
+      const int v = hist[i];
+      hist[i] = run;
+      run += v;
+    }
+    total_s[e] = run;
+    nblk[e] = (run + block_m - 1) / block_m;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // E <= 1024: a serial scan is a few microseconds at most
+    int run = 0;
+    for (int e = 0; e < num_experts; ++e) {
+      scan[e] = run;
+      run += nblk[e];
+    }
+    num_post_padded[0] = run * block_m;
+    for (int64_t b = run; b < capacity_blocks; ++b) block_expert[b] = -1;
+  }
+  __syncthreads();
+  const int32_t pad = static_cast<int32_t>(num_routes);
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
+    blk_off[e] = scan[e];
+    for (int b = 0; b < nblk[e]; ++b) block_expert[scan[e] + b] = e;
+    const int64_t beg = static_cast<int64_t>(scan[e]) * block_m + total_s[e];
+    const int64_t end = static_cast<int64_t>(scan[e] + nblk[e]) * block_m;
+    for (int64_t i = beg; i < end; ++i) sorted_ids[i] = pad;
+  }
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_scatter_kernel(
+    const void* __restrict__ ids, int ids_dtype, int64_t num_routes, int num_experts,
+    int expert_offset, int block_m, const int32_t* __restrict__ rank, const int32_t* __restrict__ hist,
+    const int32_t* __restrict__ blk_off, int32_t* __restrict__ sorted_ids) {
+  const int64_t r = blockIdx.x * static_cast<int64_t>(kRouteThreads) + threadIdx.x;
+  if (r >= num_routes) return;
+  const int rk = rank[r];
+  if (rk < 0) return;
+  const int e = load_expert(ids, ids_dtype, r) - expert_offset;
+  const int64_t pos = static_cast<int64_t>(blk_off[e]) * block_m +
+                      hist[static_cast<int64_t>(blockIdx.x) * num_experts + e] + rk;
+  sorted_ids[pos] = static_cast<int32_t>(r);
+}
+
+// ---------------------------------------------------------------------------
+// K5: out[t, :] = bf16( sum_j float(rows[t*top_k + j, :]) ), FP32 accumulation
+// in j order.  8 columns (16 bytes) per thread.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) combine_topk_kernel(const __nv_bfloat16* __restrict__ rows,
+                                                           __nv_bfloat16* __restrict__ out,
+                                                           int64_t num_tokens, int top_k,
+                                                           int64_t hidden) {
+  const int64_t vec_per_row = hidden / 8;
+  const int64_t total = num_tokens * vec_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec_per_row, v = i % vec_per_row;
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
+    for (int j = 0; j < top_k; ++j) {
+      const uint4 q = *reinterpret_cast<const uint4*>(rows + ((t * top_k + j) * hidden) + v * 8);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        acc[2 * c] += __uint_as_float(w[c] << 16);
+        acc[2 * c + 1] += __uint_as_float(w[c] & 0xFFFF0000u);
+      }
+    }
+    uint4 o;
+    o.x = f32x2_to_bf16x2(acc[0], acc[1]);
+    o.y = f32x2_to_bf16x2(acc[2], acc[3]);
+    o.z = f32x2_to_bf16x2(acc[4], acc[5]);
+    o.w = f32x2_to_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + t * hidden + v * 8) = o;
+  }
+}
+
+}  // namespace mx
