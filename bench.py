@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MXFP4 backend (prints ONE JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Headline workload (the large-prefill dense linear):
+qkv_proj M=4096, K=2048, N=5120 through the fused W4A16 kernel (weights
+decoded inside the GEMM producer).  A "step" is one pass of the linear over
+one batch.  ``value`` is the whole-job TFLOP/s (2*M*N*K per step) with the
+inputs resident in HBM, timed with CUDA events on the launching stream over
+exactly K steps (CUDA-graph replays rotating 4 input sets of 64 MB each, so
+the working set of consecutive steps exceeds the 126 MB L2).  ``e2e`` times the
+same metric through the public operator call with pinned HOST buffers (the
+activation copy in, the output copy out, every step).
+
+At N=1 the other BASELINE configurations are measured as ``extra`` entries
+(o_proj, the decode sweep, the safe mode, the MoE layer of config 2).  With
+N>1 ranks (torchrun, NCCL) the headline is the column-sharded linear: each
+rank owns N/G output columns and an NCCL all-gather assembles the output
+(strong scaling, total work fixed).
+
+``--impl reference`` times the reference's safe path restated with PyTorch CPU
+ops (oracle/ref_cpu.py) on this machine's host cores for the same workload; the
+reference checkout itself does not exist on the GPU box.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "mxfp4-gfx936_b200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "MXFP4 GEMM TFLOP/s & MoE-layer tokens/s at 1/2/4/8 B200; % of roofline"
+QKV = (4096, 5120, 2048)        # M, N, K
+OPROJ = (4096, 2048, 4096)
+DECODE_M = (1, 8, 64, 370)
+MOE = dict(t=4096, h=2048, e=128, k=8, inter=768)
+
+
+def _load(name, path):
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(key):
+    p = ROOT / "profiles" / "traffic.json"
+    if p.is_file():
+        return json.loads(p.read_text()).get(key)
+    return None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Polls SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.sm_max = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.h = self._handle_for(pynvml, device_index)
+            self.nvml = pynvml
+            self.sm_max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # no NVML: report that, do not fail the bench
+            self.nvml, self.error = None, str(exc)
+
+    @staticmethod
+    def _handle_for(pynvml, device_index):
+        # match the CUDA device to its NVML handle by UUID (CUDA_VISIBLE_DEVICES
+        # may renumber devices); fall back to the same index
+        try:
+            want = str(torch.cuda.get_device_properties(device_index).uuid).lower()
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = (u.decode() if isinstance(u, bytes) else u).lower()
+                if u.endswith(want):
+                    return h
+        except Exception:
+            pass
+        return pynvml.nvmlDeviceGetHandleByIndex(device_index)
+
+    def _run(self):
+        n = self.nvml
+        get_r = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or n.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM))
+                bits = get_r(self.h)
+                for b, name in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def result(self):
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": self.error}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.sm_max,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- helpers
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_linear_inputs(m, n, k, seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(m, k, generator=g, device=device).to(torch.bfloat16)
+    w = torch.randint(0, 256, (n, k // 2), generator=g, device=device, dtype=torch.uint8)
+    s = torch.randint(118, 131, (n, k // 32), generator=g, device=device, dtype=torch.uint8)
+    return x, w, s
+
+
+def graphs_for(fn, sets, stream):
+    """One CUDA graph per input set, each holding one step."""
+    gs = []
+    for args in sets:
+        fn(*args)  # warm the allocator and one-time attributes outside capture
+    torch.cuda.synchronize()
+    for args in sets:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn(*args)
+        gs.append(g)
+    torch.cuda.synchronize()
+    return gs
+
+
+def time_graphs(gs, steps, warmup, barrier=None, sampler=None):
+    """Replay rotating graphs; returns ms per step measured with CUDA events."""
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        gs[i % len(gs)].replay()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        start.record(stream)
+        for i in range(steps):
+            gs[i % len(gs)].replay()
+        end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    return start.elapsed_time(end) / steps
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def set_backend(name):
+    os.environ["MXFP4_GFX936_BACKEND"] = name
+
+
+# ----------------------------------------------------------------------------- workloads
+def bench_linear(soft, shape, steps, warmup, n_sets, backend, device, sampler=None, seed0=0):
+    m, n, k = shape
+    set_backend(backend)
+    sets = [make_linear_inputs(m, n, k, seed0 + i, device) for i in range(n_sets)]
+    gs = graphs_for(lambda x, w, s: soft.linear_mxfp4_soft(x, w, s), sets, torch.cuda.Stream())
+    ms = time_graphs(gs, steps, warmup, sampler=sampler)
+    del gs, sets
+    return ms
+
+
+def bench_e2e_linear(soft, shape, steps, warmup, device):
+    m, n, k = shape
+    set_backend("fused")
+    x, w, s = make_linear_inputs(m, n, k, 123, device)
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+
+    def step():
+        xd = x_host.to(device, non_blocking=True)
+        y = soft.linear_mxfp4_soft(xd, w, s)
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    end.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3 / steps
+    ms = start.elapsed_time(end) / steps
+    return max(ms, wall), x_host.numel() * 2, y_host.numel() * 2
+
+
+def make_moe_inputs(device, seed=0, **cfg):
+    t, h, e, k, inter = cfg["t"], cfg["h"], cfg["e"], cfg["k"], cfg["inter"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(t, h, generator=g, device=device).to(torch.bfloat16)
+    w13 = torch.randint(0, 256, (e, 2 * inter, h // 2), generator=g, device=device, dtype=torch.uint8)
+    s13 = torch.randint(118, 131, (e, 2 * inter, h // 32), generator=g, device=device, dtype=torch.uint8)
+    w2 = torch.randint(0, 256, (e, h, inter // 2), generator=g, device=device, dtype=torch.uint8)
+    s2 = torch.randint(118, 131, (e, h, inter // 32), generator=g, device=device, dtype=torch.uint8)
+    logits = torch.randn(t, e, generator=g, device=device)
+    tw, tid = torch.topk(torch.softmax(logits, -1), k, dim=-1)
+    tw = tw / tw.sum(-1, keepdim=True)
+    return x, w13, s13, w2, s2, tw, tid
+
+
+def bench_moe(soft, steps, warmup, device):
+    sets = [make_moe_inputs(device, seed=i, **MOE) for i in range(2)]
+    gs = graphs_for(lambda *a: soft.moe_layer_mxfp4(*a), sets, torch.cuda.Stream())
+    ms = time_graphs(gs, steps, warmup)
+    del gs, sets
+    return ms
+
+
+def moe_flops(cfg=MOE):
+    return 2.0 * cfg["t"] * cfg["k"] * (cfg["h"] * 2 * cfg["inter"] + cfg["inter"] * cfg["h"])
+
+
+def linear_bytes(m, n, k):
+    return 2 * m * k + n * k // 2 + n * k // 32 + 2 * m * n
+
+
+# ----------------------------------------------------------------------------- CPU side
+def cpu_linear_tflops(shape, steps, warmup, budget_s=25.0):
+    """The reference's safe linear restated with torch CPU ops, all host threads."""
+    ref = _load("mxfp4_ref_cpu", ROOT / "oracle" / "ref_cpu.py")
+    torch.set_num_threads(os.cpu_count() or 1)
+    m, n, k = shape
+    g = torch.Generator().manual_seed(0)
+    w = torch.randint(0, 256, (n, k // 2), generator=g, dtype=torch.uint8)
+    s = torch.randint(118, 131, (n, k // 32), generator=g, dtype=torch.uint8)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    t0 = time.perf_counter()
+    ref.linear(x, w, s)
+    one = time.perf_counter() - t0
+    m_used = m
+    if one * (steps + warmup) > budget_s:  # bounded sample: fewer rows, same weights
+        m_used = max(64, int(m * budget_s / (one * (steps + warmup))) // 64 * 64)
+        x = x[:m_used].contiguous()
+    for _ in range(warmup):
+        ref.linear(x, w, s)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        ref.linear(x, w, s)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    mean = sum(times) / len(times)
+    flops = 2.0 * m_used * n * k
+    return {"tflops_best": flops / best / 1e12, "tflops_mean": flops / mean / 1e12, "ms_mean": mean * 1e3,
+            "m_used": m_used, "threads": torch.get_num_threads()}
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    r = cpu_linear_tflops(QKV, args.steps, args.warmup, budget_s=150.0)
+    m, n, k = QKV
+    sample = f"qkv_proj {r['m_used']}x{n}x{k} (rows sampled from M={m})" if r["m_used"] != m else f"qkv_proj {m}x{n}x{k}"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": r["tflops_mean"], "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_mean"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config1_qkv_prefill", "M": m, "N": n, "K": k},
+        "cpu_baseline": {"value": r["tflops_mean"], "unit": "TFLOP/s", "cores": r["threads"], "kind": "port",
+                         "sample": sample + "; reference safe path (dequant + torch.matmul) as torch CPU ops"},
+        "e2e": {"value": r["tflops_mean"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-extra", action="store_true", help="skip the non-headline configurations")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    soft = _load("moe_op_mxfp4_soft", PKG / "moe_op_mxfp4_soft.py")
+    pk, pk_kind = peaks()
+    m, n, k = QKV
+
+    if world > 1:
+        return run_sharded(args, soft, world, rank, device, pk, pk_kind)
+
+    sampler = ClockSampler(local)
+    ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "fused", device, sampler=sampler)
+    flops = 2.0 * m * n * k
+    tflops = flops / (ms * 1e-3) / 1e12
+    e2e_ms, h2d, d2h = bench_e2e_linear(soft, QKV, max(10, args.steps // 4), args.warmup, device)
+
+    line = {
+        "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE config-1 distributions, seeded)",
+        "config": {"workload": "config1_qkv_prefill", "M": m, "N": n, "K": k, "backend": "fused",
+                   "l2": "4 rotating input sets of 64 MB (working set > 126 MB L2)", "timing": "CUDA-graph replays, CUDA events",
+                   "parallelism": "single GPU"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / pk["bf16_tflops"], "traffic": profile_traffic("linear_fused_qkv"),
+                     "peak_source": f"{pk_kind} bf16 burst"},
+        "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "clocks": sampler.result(),
+    }
+
+    if not args.no_extra:
+        extra = {}
+        ms_o = bench_linear(soft, OPROJ, 100, 10, 4, "fused", device, seed0=10)
+        fo = 2.0 * OPROJ[0] * OPROJ[1] * OPROJ[2]
+        extra["config1_oproj_fused"] = {"ms": ms_o, "tflops": fo / ms_o / 1e9, "frac_bf16": fo / ms_o / 1e9 / pk["bf16_tflops"]}
+        ms_s = bench_linear(soft, QKV, 100, 10, 4, "safe", device, seed0=20)
+        extra["config1_qkv_safe"] = {"ms": ms_s, "tflops": flops / ms_s / 1e9}
+        for dm in DECODE_M:
+            shape = (dm, n, k)
+            ms_d = bench_linear(soft, shape, 400, 20, 32, "fused", device, seed0=100 + dm)
+            byts = linear_bytes(dm, n, k)
+            extra[f"decode_qkv_m{dm}"] = {"ms": ms_d, "us": ms_d * 1e3, "gbs": byts / ms_d / 1e6,
+                                          "frac_hbm": byts / ms_d / 1e6 / pk["hbm_gbs"],
+                                          "tflops": 2.0 * dm * n * k / ms_d / 1e9}
+        ms_m = bench_moe(soft, 20, 3, device)
+        fm = moe_flops()
+        extra["config2_moe_layer"] = {"ms": ms_m, "tokens_per_s": MOE["t"] / (ms_m * 1e-3), "tflops": fm / ms_m / 1e9,
+                                      "frac_bf16": fm / ms_m / 1e9 / pk["bf16_tflops"], "launches_per_step": 6}
+        line["extra"] = extra
+
+    cb = cpu_linear_tflops(QKV, 2, 1, budget_s=25.0)
+    line["cpu_baseline"] = {"value": cb["tflops_mean"], "unit": "TFLOP/s", "cores": cb["threads"], "kind": "port",
+                            "sample": f"qkv_proj {cb['m_used']}x{n}x{k}, 2 timed steps; reference safe path "
+                                      "(dequant + torch.matmul) as torch CPU ops (oracle/ref_cpu.py)"}
+    status = soft.device_status()
+    if status:
+        line["device_status"] = status
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_sharded(args, soft, world, rank, device, pk, pk_kind):
+    import datetime
+
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    cp = _load("mxfp4_column_parallel", PKG / "column_parallel.py")
+    m, n, k = QKV
+    set_backend("fused")
+    sets = []
+    for i in range(4):
+        x, w, s = make_linear_inputs(m, n, k, i, device)  # same full weight on every rank
+        sets.append((x, cp.ColumnParallelLinear.from_full(w, s, rank, world)))
+    barrier = lambda: dist.barrier(device_ids=[device.index])  # noqa: E731
+    gs = graphs_for(lambda x, layer: layer(x), sets, torch.cuda.Stream())
+    ms_local = time_graphs(gs, args.steps, args.warmup, barrier=barrier)
+    t = torch.tensor([ms_local], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    flops = 2.0 * m * n * k
+    tflops = flops / (ms * 1e-3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE config-1 distributions, seeded)",
+            "config": {"workload": "config1_qkv_prefill", "M": m, "N": n, "K": k, "backend": "fused",
+                       "parallelism": f"tp{world} column-sharded + NCCL all-gather",
+                       "l2": "4 rotating input sets"},
+            "roofline": None, "gpu_launches": args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    del gs
+    dist.barrier(device_ids=[device.index])
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -134,3 +134,43 @@ def test_ocp_quantizer_round_trip_properties():
     assert s[0, 0] == 127
     got = O.dequant(p, s, "fp32")[0, 1:9]
     np.testing.assert_array_equal(got, [0.0, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0, 6.0])
+
+
+# --------------------------------------------------------------------------
+# the PyTorch-CPU port used as bench.py's CPU baseline (oracle/ref_cpu.py)
+# --------------------------------------------------------------------------
+import torch  # noqa: E402
+
+from _paths import ROOT, load_by_path  # noqa: E402
+
+R = load_by_path("mxfp4_ref_cpu", ROOT / "oracle" / "ref_cpu.py")
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16", "fp16"])
+def test_cpu_port_dequant_bit_exact(dtype):
+    g = golden("dequant")
+    tdt = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
+    out = R.dequant(torch.from_numpy(g["packed"]), torch.from_numpy(g["scales"]), tdt)
+    assert same_bits(out.float().numpy(), _unbits(g[f"out_{dtype}"], dtype))
+
+
+@pytest.mark.parametrize("case", range(6))
+def test_cpu_port_linear(case):
+    g = golden("linear")
+    pre = f"c{case}_"
+    dt = str(g[pre + "dtype"])
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float16
+    x = torch.from_numpy(g[pre + "x"].view(np.int16)).view(tdt)
+    bias = torch.from_numpy(g[pre + "bias"].view(np.int16)).view(tdt) if pre + "bias" in g.files else None
+    y = R.linear(x, torch.from_numpy(g[pre + "w"]), torch.from_numpy(g[pre + "s"]), bias)
+    ok, err, bound, rel = O.check_close(y.float().numpy(), _unbits(g[pre + "y"], dt))
+    assert ok, (err, bound, rel)
+
+
+def test_cpu_port_moe_layer():
+    g = golden("moe_layer")
+    x = torch.from_numpy(g["x"].view(np.int16)).view(torch.bfloat16)
+    y = R.moe_layer(x, *(torch.from_numpy(g[k]) for k in ("w13", "s13", "w2", "s2")),
+                    torch.from_numpy(g["tw"]), torch.from_numpy(g["tid"]))
+    ok, err, bound, rel = O.check_close(y.float().numpy(), bf16_to_f32(g["y"]))
+    assert ok, (err, bound, rel)
