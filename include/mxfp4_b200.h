@@ -133,6 +133,24 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
                     int64_t n, int64_t k, int mul_routed_weight, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference.  mxfp4_fused_moe for callers that cannot  */
+/* allocate device memory at call time -- e.g. a plugin host or graph        */
+/* executor that owns every buffer after initialisation, or a fixed memory   */
+/* plan replayed under stream capture -- and so cannot provide `workspace`.  */
+/* Same arguments and result as mxfp4_fused_moe without the workspace: the  */
+/* scratch comes from an 8 MiB static device array of the library (held on  */
+/* every GPU that loads it until exit).  A request needing more scratch than */
+/* that (mxfp4_fused_moe_workspace_size() > 8 MiB) returns                   */
+/* MXFP4_ERR_WORKSPACE.  The first call on a device looks up the array's     */
+/* device address, so make it before any stream capture.  All calls share    */
+/* the array: calls that overlap on the GPU (other streams, other host       */
+/* threads) race and must be serialised by the caller.                      */
+int mxfp4_fused_moe_noalloc(const void* A, int a_dtype, const void* a_mx_scale, const void* B,
+                            const void* B_mx_scale, const float* a_scale, const float* b_scale,
+                            const void* topk_weights, int w_dtype, const void* topk_ids, int ids_dtype,
+                            void* C, int c_dtype, int64_t num_tokens, int top_k, int num_experts,
+                            int64_t n, int64_t k, int mul_routed_weight, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* K3+K5 -- MoE layer.  Replaces _moe_apply (vllm:233-265) with the W4A16    */
 /* MXFP4 experts: gate_up = x . W13[e]^T (gate = first `inter` rows), h =    */

@@ -219,6 +219,43 @@ int grouped_gemm(bool fp16, const CUtensorMap& ta, const CUtensorMap& tb, const 
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Static scratch for mxfp4_fused_moe_noalloc.  Some callers cannot allocate
+// device memory when they call into this library (a plugin host or graph
+// executor that owns every buffer after initialisation, a fixed memory plan
+// replayed under stream capture), so that entry point takes its routing
+// scratch from this array instead of a caller workspace.  Every GPU that loads
+// the library holds these bytes until the process exits.  In host code the
+// array's name is only a host-side stand-in: its device address comes from
+// cudaGetSymbolAddress, looked up once per device.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of g_noalloc_scratch for the current device; the first call
+// on a device does the lookup (so it must not happen inside a stream capture).
+int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  MX_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(MXFP4_ERR_UNSUPPORTED_DEVICE, "device index out of range");
+  std::lock_guard<std::mutex> lk(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(MXFP4_ERR_CUDA, std::string("cudaGetSymbolAddress(g_noalloc_scratch): ") + cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return MXFP4_OK;
+}
+
+}  // namespace
+
 // ===========================================================================
 // C ABI
 // ===========================================================================
@@ -486,6 +523,32 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   p.c_stride_j = n;
   p.vec_ok = aligned(C, 16) && (n * esz) % 16 == 0;
   return grouped_gemm<A_GATHER, EPI_MOE>(cdt == MXFP4_DTYPE_F16, ta, tb, p, info.sms, s);
+}
+
+// Same operation as mxfp4_fused_moe, with its scratch taken from the static
+// g_noalloc_scratch array instead of a caller workspace: no cudaMalloc, no
+// cudaFree, no allocating library call.  Requests whose scratch would exceed
+// kNoAllocScratchBytes are rejected.  All calls share the array, so calls that
+// overlap on the GPU race; nothing in it needs to start at zero (every byte a
+// call reads was written earlier in the same call).
+int mxfp4_fused_moe_noalloc(const void* A, int a_dtype, const void* a_mx_scale, const void* B,
+                            const void* B_mx_scale, const float* a_scale, const float* b_scale,
+                            const void* topk_weights, int w_dtype, const void* topk_ids, int ids_dtype,
+                            void* C, int c_dtype, int64_t num_tokens, int top_k, int num_experts,
+                            int64_t n, int64_t k, int mul_routed_weight, void* stream) {
+  if (num_tokens < 0 || top_k <= 0 || num_experts <= 0 || num_experts > kMaxExperts)
+    return fail(MXFP4_ERR_INVALID_ARGUMENT, "bad sizes");
+  const size_t need = mxfp4_fused_moe_workspace_size(num_tokens, top_k, num_experts, n, k, a_dtype, c_dtype);
+  if (need > kNoAllocScratchBytes)
+    return fail(MXFP4_ERR_WORKSPACE, "mxfp4_fused_moe_noalloc needs " + std::to_string(need) +
+                                         " scratch bytes, more than its static " +
+                                         std::to_string(kNoAllocScratchBytes) +
+                                         "-byte array; call mxfp4_fused_moe with a workspace instead");
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  return mxfp4_fused_moe(A, a_dtype, a_mx_scale, B, B_mx_scale, a_scale, b_scale, topk_weights, w_dtype,
+                         topk_ids, ids_dtype, C, c_dtype, num_tokens, top_k, num_experts, n, k,
+                         mul_routed_weight, scratch, kNoAllocScratchBytes, stream);
 }
 
 size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t hidden,

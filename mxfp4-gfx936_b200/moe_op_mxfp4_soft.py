@@ -109,6 +109,11 @@ _SIGNATURES = {
         [_VP, _INT, _VP, _VP, _VP, _VP, _VP, _VP, _INT, _VP, _INT, _VP, _INT, _I64, _INT, _INT, _I64, _I64,
          _INT, _VP, _SZ, _VP],
     ),
+    "mxfp4_fused_moe_noalloc": (
+        _INT,
+        [_VP, _INT, _VP, _VP, _VP, _VP, _VP, _VP, _INT, _VP, _INT, _VP, _INT, _I64, _INT, _INT, _I64, _I64,
+         _INT, _VP],
+    ),
     "mxfp4_moe_layer_workspace_size": (_SZ, [_I64, _INT, _INT, _I64, _I64]),
     "mxfp4_moe_layer": (
         _INT,
