@@ -46,6 +46,8 @@ QKV = (4096, 5120, 2048)        # M, N, K
 OPROJ = (4096, 2048, 4096)
 DECODE_M = (1, 8, 64, 370)
 MOE = dict(t=4096, h=2048, e=128, k=8, inter=768)
+W4A4 = (8192, 4096, 4096)       # M, N, K
+FP4_NOMINAL_TFLOPS = 9000.0     # datasheet dense FP4; not measured on this pool
 
 
 def _load(name, path):
@@ -267,6 +269,23 @@ def bench_moe(soft, steps, warmup, device):
     return ms
 
 
+def bench_w4a4(soft, steps, warmup, device):
+    m, n, k = W4A4
+    sets = []
+    for i in range(2):
+        g = torch.Generator(device=device).manual_seed(50 + i)
+        xa = torch.randn(m, k, generator=g, device=device).to(torch.bfloat16)
+        xb = torch.randn(n, k, generator=g, device=device).to(torch.bfloat16)
+        a, sa = soft.quantize_mxfp4(xa)
+        b, sb = soft.quantize_mxfp4(xb)
+        sets.append((a, sa, b, sb))
+        del xa, xb
+    gs = graphs_for(lambda *t: soft.gemm_mxfp4_w4a4(*t), sets, torch.cuda.Stream())
+    ms = time_graphs(gs, steps, warmup)
+    del gs, sets
+    return ms
+
+
 def moe_flops(cfg=MOE):
     return 2.0 * cfg["t"] * cfg["k"] * (cfg["h"] * 2 * cfg["inter"] + cfg["inter"] * cfg["h"])
 
@@ -390,6 +409,12 @@ def main():
         fm = moe_flops()
         extra["config2_moe_layer"] = {"ms": ms_m, "tokens_per_s": MOE["t"] / (ms_m * 1e-3), "tflops": fm / ms_m / 1e9,
                                       "frac_bf16": fm / ms_m / 1e9 / pk["bf16_tflops"], "launches_per_step": 6}
+        ms_w = bench_w4a4(soft, 50, 5, device)
+        fw = 2.0 * W4A4[0] * W4A4[1] * W4A4[2]
+        extra["config3_w4a4"] = {"ms": ms_w, "tflops": fw / ms_w / 1e9,
+                                 "frac_fp4_nominal": fw / ms_w / 1e9 / FP4_NOMINAL_TFLOPS,
+                                 "vs_bf16_peak": fw / ms_w / 1e9 / pk["bf16_tflops"],
+                                 "launches_per_step": 3}
         line["extra"] = extra
 
     cb = cpu_linear_tflops(QKV, 2, 1, budget_s=25.0)

@@ -94,6 +94,29 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
                        size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Quantizer -- BF16/F32 -> packed MXFP4 + E8M0 (the W4A4 configuration's   */
+/* OCP rounding; the reference only has a test quantizer, test:28-60).       */
+/* Per 32 values: q = fl32(max|x| / 6), scale code = clamp(floor(log2 q) +  */
+/* 127, 0, 254) (0 for an all-zero block), element = RNE(x * 2^(127-code))   */
+/* on the E2M1 grid, ties to the even code, saturated at +-6, zero unsigned. */
+/* x: [rows, k] with row stride ldx elements; packed [rows, k/2];            */
+/* scales [rows, k/32].  k % 32 == 0.                                       */
+int mxfp4_quantize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t k, void* packed,
+                   void* scales, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* K2 -- W4A4 GEMM on the block-scaled tensor cores (tcgen05 kind::mxf4).  */
+/* Replaces the packed-activation branch of soft:468-475 (dequant A, dequant */
+/* B, one matmul) and the native dot_scaled kernel of aiter:304-338:         */
+/* out[m, n] = round(sum_k deq(A)[m,k] * deq(B)[n,k]), FP32 accumulation.    */
+/* a: [m, k/2] u8, a_scales [m, k/32]; b: [n, k/2] u8, b_scales [n, k/32]; */
+/* out [m, n] (BF16, F16 or F32); all contiguous; k % 128 == 0.              */
+size_t mxfp4_gemm_w4a4_workspace_size(int64_t m, int64_t n, int64_t k);
+int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const void* b_scales, void* out,
+                    int out_dtype, int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* K4 -- device routing.  Replaces _make_routing (vllm:119-146) without its  */
 /* host sync.  Route r = t*top_k + j of topk_ids[num_tokens, top_k] (I32 or  */
 /* I64) goes to local expert e = id - expert_offset when 0 <= e <           */

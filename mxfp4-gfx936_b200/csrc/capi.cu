@@ -7,6 +7,7 @@
 
 #include "elementwise.cuh"
 #include "gemm.cuh"
+#include "gemm_w4a4.cuh"
 
 using namespace mx;
 
@@ -549,6 +550,96 @@ int mxfp4_fused_moe_noalloc(const void* A, int a_dtype, const void* a_mx_scale, 
   return mxfp4_fused_moe(A, a_dtype, a_mx_scale, B, B_mx_scale, a_scale, b_scale, topk_weights, w_dtype,
                          topk_ids, ids_dtype, C, c_dtype, num_tokens, top_k, num_experts, n, k,
                          mul_routed_weight, scratch, kNoAllocScratchBytes, stream);
+}
+
+int mxfp4_quantize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t k, void* packed,
+                   void* scales, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(x && packed && scales, "null pointer");
+  MX_CHECK(x_dtype == MXFP4_DTYPE_BF16 || x_dtype == MXFP4_DTYPE_F32, "quantizer input must be BF16 or F32");
+  MX_CHECK(rows >= 0 && k > 0 && k % 32 == 0 && ldx >= k, "K must be a positive multiple of 32");
+  MX_CHECK(aligned(x, 16) && (ldx * elem_size(x_dtype)) % 16 == 0 && aligned(packed, 16),
+           "quantizer operands must be 16-byte aligned");
+  const int64_t nb = rows * (k / 32);
+  if (nb == 0) return MXFP4_OK;
+  const int grid = static_cast<int>(std::min<int64_t>((nb + 255) / 256, int64_t(info.sms) * 8));
+  cudaStream_t s = as_stream(stream);
+  if (x_dtype == MXFP4_DTYPE_BF16)
+    quantize_kernel<MXFP4_DTYPE_BF16><<<grid, 256, 0, s>>>(x, ldx, rows, k, static_cast<uint8_t*>(packed),
+                                                          static_cast<uint8_t*>(scales));
+  else
+    quantize_kernel<MXFP4_DTYPE_F32><<<grid, 256, 0, s>>>(x, ldx, rows, k, static_cast<uint8_t*>(packed),
+                                                         static_cast<uint8_t*>(scales));
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+size_t mxfp4_gemm_w4a4_workspace_size(int64_t m, int64_t n, int64_t k) {
+  const int64_t kch = k / 128;
+  const int64_t mrb = (m + kW4BM - 1) / kW4BM;
+  const int64_t nrb = 2 * ((n + kW4BN - 1) / kW4BN);
+  return align_up(static_cast<size_t>(mrb * kch * 512), 256) + align_up(static_cast<size_t>(nrb * kch * 512), 256);
+}
+
+int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const void* b_scales, void* out,
+                    int out_dtype, int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  if (int rc = check_scales_layout(k)) return rc;
+  MX_CHECK(a && a_scales && b && b_scales && out, "null pointer");
+  MX_CHECK(out_dtype == MXFP4_DTYPE_BF16 || out_dtype == MXFP4_DTYPE_F16 || out_dtype == MXFP4_DTYPE_F32,
+           "W4A4 output must be BF16, F16 or F32");
+  MX_CHECK(m >= 0 && n > 0 && m < (int64_t(1) << 31) && n < (int64_t(1) << 31), "bad M/N");
+  const size_t need = mxfp4_gemm_w4a4_workspace_size(m, n, k);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(MXFP4_ERR_WORKSPACE, "W4A4 GEMM needs " + std::to_string(need) + " workspace bytes");
+  if (m == 0) return MXFP4_OK;
+  cudaStream_t s = as_stream(stream);
+  const int kch = static_cast<int>(k / 128);
+  const int mrb = static_cast<int>((m + kW4BM - 1) / kW4BM);
+  const int nrb = static_cast<int>(2 * ((n + kW4BN - 1) / kW4BN));
+  uint8_t* sfa = static_cast<uint8_t*>(workspace);
+  uint8_t* sfb = sfa + align_up(static_cast<size_t>(mrb) * kch * 512, 256);
+  {
+    const int64_t wa = static_cast<int64_t>(mrb) * 128 * kch, wb = static_cast<int64_t>(nrb) * 128 * kch;
+    sf_block_kernel<<<static_cast<int>(std::min<int64_t>((wa + 255) / 256, info.sms * 8)), 256, 0, s>>>(
+        static_cast<const uint8_t*>(a_scales), k / 32, static_cast<int>(m), kch, mrb, sfa);
+    sf_block_kernel<<<static_cast<int>(std::min<int64_t>((wb + 255) / 256, info.sms * 8)), 256, 0, s>>>(
+        static_cast<const uint8_t*>(b_scales), k / 32, static_cast<int>(n), kch, nrb, sfb);
+    MX_CUDA(cudaGetLastError());
+  }
+  CUtensorMap ta, tb;
+  if (int rc = make_map_2d(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, m, k / 2, 128, kW4BM,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = make_map_2d(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, k / 2, 128, kW4BN,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  W4A4Params p{};
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.num_m_blocks = mrb;
+  p.num_n_blocks = static_cast<int>((n + kW4BN - 1) / kW4BN);
+  p.sfa_blk = sfa;
+  p.sfb_blk = sfb;
+  p.out = out;
+  p.ldo = n;
+  p.out_dtype = out_dtype;
+  p.vec_ok = aligned(out, 16) && (n * elem_size(out_dtype)) % 16 == 0;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(mxfp4_w4a4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kW4SmemBytes);
+  });
+  MX_CUDA(attr_err);
+  const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, info.sms));
+  mxfp4_w4a4_kernel<<<grid, 256, kW4SmemBytes, s>>>(ta, tb, p);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
 }
 
 size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t hidden,

@@ -100,6 +100,9 @@ _SIGNATURES = {
         _INT,
         [_VP, _INT, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64, _INT, _VP, _SZ, _VP],
     ),
+    "mxfp4_quantize": (_INT, [_VP, _INT, _I64, _I64, _I64, _VP, _VP, _VP]),
+    "mxfp4_gemm_w4a4_workspace_size": (_SZ, [_I64, _I64, _I64]),
+    "mxfp4_gemm_w4a4": (_INT, [_VP, _VP, _VP, _VP, _VP, _INT, _I64, _I64, _I64, _VP, _SZ, _VP]),
     "mxfp4_moe_route_capacity": (_I64, [_I64, _INT, _INT]),
     "mxfp4_moe_route_workspace_size": (_SZ, [_I64, _INT]),
     "mxfp4_moe_route": (_INT, [_VP, _INT, _I64, _INT, _INT, _INT, _INT, _VP, _VP, _VP, _I64, _VP, _SZ, _VP]),
@@ -475,6 +478,65 @@ def moe_layer_mxfp4(x: torch.Tensor, w13: torch.Tensor, w13_scale: torch.Tensor,
             _ptr(xs), _ptr(_dense(w13)), _ptr(_dense(w13_scale)), _ptr(_dense(w2)), _ptr(_dense(w2_scale)),
             _ptr(tw), _DTYPE_CODES[tw.dtype], _ptr(tid), _DTYPE_CODES[tid.dtype], _ptr(out),
             t, top_k, num_experts, hidden, inter, _ptr(ws), ws_bytes, _stream(device)))
+    return out
+
+
+def quantize_mxfp4(x: torch.Tensor):
+    """BF16/FP32 -> (packed uint8 [..., K/2], E8M0 scales uint8 [..., K/32]).
+
+    OCP MXFP4 with the W4A4 configuration's rounding: scale code
+    floor(log2(fl32(max|x|/6))) + 127 per 32 values, elements rounded to
+    nearest-even on the E2M1 grid and saturated at 6.
+    """
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"x must be bf16 or fp32, got {x.dtype}")
+    k = x.shape[-1]
+    if k % 32:
+        raise ValueError(f"K must be divisible by 32, got {k}")
+    device = _require_cuda(x)
+    x2 = _dense(x.reshape(-1, k))
+    rows = x2.shape[0]
+    packed = torch.empty((*x.shape[:-1], k // 2), dtype=torch.uint8, device=device)
+    scales = torch.empty((*x.shape[:-1], k // 32), dtype=torch.uint8, device=device)
+    if rows:
+        with torch.cuda.device(device):
+            _check(_load_library().mxfp4_quantize(_ptr(x2), _DTYPE_CODES[x.dtype], k, rows, k, _ptr(packed),
+                                                  _ptr(scales), _stream(device)))
+    return packed, scales
+
+
+def gemm_mxfp4_w4a4(a_packed: torch.Tensor, a_scales: torch.Tensor, b_packed: torch.Tensor,
+                    b_scales: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """W4A4: ``dequant(A) @ dequant(B)^T`` on the block-scaled tensor cores.
+
+    The reference's packed-activation semantics (soft:468-475: both operands
+    dequantised, one matmul with FP32 accumulation), computed natively with
+    tcgen05 ``kind::mxf4`` and one E8M0 scale per 32 values on each side.
+    """
+    for name, t in (("a_packed", a_packed), ("a_scales", a_scales), ("b_packed", b_packed), ("b_scales", b_scales)):
+        if t.dtype != torch.uint8:
+            raise TypeError(f"{name} must be uint8, got {t.dtype}")
+    if a_packed.ndim != 2 or b_packed.ndim != 2:
+        raise ValueError("W4A4 operands must be 2D")
+    if out_dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        raise TypeError(f"unsupported output dtype {out_dtype}")
+    m, k = a_packed.shape[0], a_packed.shape[1] * 2
+    n = b_packed.shape[0]
+    if b_packed.shape[1] * 2 != k:
+        raise ValueError("A and B must have the same K")
+    if k % 128:
+        raise ValueError(f"logical K must be divisible by 128, got {k}")
+    if tuple(a_scales.shape) != (m, k // 32) or tuple(b_scales.shape) != (n, k // 32):
+        raise ValueError("one E8M0 scale is required for every 32 MXFP4 values")
+    device = _require_cuda(a_packed, a_scales, b_packed, b_scales)
+    lib = _load_library()
+    out = torch.empty((m, n), dtype=out_dtype, device=device)
+    ws_bytes = lib.mxfp4_gemm_w4a4_workspace_size(m, n, k)
+    ws = _workspace(ws_bytes, device)
+    a, sa, b, sb = _dense(a_packed), _dense(a_scales), _dense(b_packed), _dense(b_scales)
+    with torch.cuda.device(device):
+        _check(lib.mxfp4_gemm_w4a4(_ptr(a), _ptr(sa), _ptr(b), _ptr(sb), _ptr(out), _DTYPE_CODES[out_dtype],
+                                   m, n, k, _ptr(ws), ws_bytes, _stream(device)))
     return out
 
 
