@@ -1,12 +1,14 @@
 // Host side of libmxfp4_b200.so: argument validation, tensor-map encoding,
 // workspace layout and kernel launches behind the C ABI in include/mxfp4_b200.h.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "elementwise.cuh"
 #include "gemm.cuh"
+#include "gemm2.cuh"
 #include "gemm_w4a4.cuh"
 
 using namespace mx;
@@ -139,6 +141,31 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
+}
+
+template <int BMODE, int DW, bool FP16>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const DenseParams& p, int clusters,
+                cudaStream_t stream) {
+  using Cfg = Pair2Cfg<BMODE, DW>;
+  auto kern = mxfp4_gemm_pair_kernel<BMODE, DW, FP16>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  });
+  MX_CUDA(attr_err);
+  kern<<<2 * clusters, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+// Decode warps per CTA of the fused pair kernel (8 or 16); MXFP4_B200_DECODE_WARPS overrides.
+int decode_warps() {
+  static int v = [] {
+    const char* e = std::getenv("MXFP4_B200_DECODE_WARPS");
+    return (e && std::atoi(e) == 8) ? 8 : 16;
+  }();
+  return v;
 }
 
 int check_scales_layout(int64_t k) {
@@ -343,31 +370,34 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   const CUtensorMapDataType xt = fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 
   CUtensorMap ta, tb;
-  if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
 
-  GemmParams p{};
+  DenseParams p{};
   p.M = static_cast<int>(m);
   p.N = static_cast<int>(n);
   p.K = static_cast<int>(k);
-  p.num_m_blocks = static_cast<int>((m + kBM - 1) / kBM);
-  p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
+  p.num_m_blocks = static_cast<int>((m + kP2BM - 1) / kP2BM);
+  p.num_n_blocks = static_cast<int>((n + kP2BN - 1) / kP2BN);
   p.w_scales = static_cast<const uint8_t*>(w_scales);
   p.lds = lds;
-  p.w_rows_per_expert = n;
   p.out = out;
   p.ldo = ldo;
   p.out_dtype = x_dtype;
   p.bias = bias;
   p.vec_ok = aligned(out, 16) && (ldo * 2) % 16 == 0;
   const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, info.sms));
+  const int clusters = static_cast<int>(std::min<int64_t>(tiles, info.sms / 2));
 
   if (mode == MXFP4_LINEAR_FUSED) {
-    if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kBK / 2,
-                             kBN / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kP2BK / 2,
+                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
-    if (fp16) return launch_gemm<A_TMA, B_DECODE, EPI_DENSE, true>(ta, tb, p, grid, s);
-    return launch_gemm<A_TMA, B_DECODE, EPI_DENSE, false>(ta, tb, p, grid, s);
+    if (decode_warps() == 8) {
+      if (fp16) return launch_pair<B_DECODE, 8, true>(ta, tb, p, clusters, s);
+      return launch_pair<B_DECODE, 8, false>(ta, tb, p, clusters, s);
+    }
+    if (fp16) return launch_pair<B_DECODE, 16, true>(ta, tb, p, clusters, s);
+    return launch_pair<B_DECODE, 16, false>(ta, tb, p, clusters, s);
   }
   // safe: explicit dequant of W into the workspace, then the same MMA pipeline
   const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
@@ -375,10 +405,10 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
     return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
   MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
   if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
-  if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if (fp16) return launch_gemm<A_TMA, B_TMA, EPI_DENSE, true>(ta, tb, p, grid, s);
-  return launch_gemm<A_TMA, B_TMA, EPI_DENSE, false>(ta, tb, p, grid, s);
+  if (fp16) return launch_pair<B_TMA, 0, true>(ta, tb, p, clusters, s);
+  return launch_pair<B_TMA, 0, false>(ta, tb, p, clusters, s);
 }
 
 int64_t mxfp4_moe_route_capacity(int64_t num_routes, int num_experts, int block_m) {

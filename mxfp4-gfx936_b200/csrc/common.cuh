@@ -14,7 +14,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
-#include "../../include/mxfp4_b200.h"
+#include "mxfp4_b200.h"  // include/ is on the include path (build_lib.py)
 
 namespace mx {
 

@@ -1,0 +1,369 @@
+// Dense W4A16 linear on CTA pairs (tcgen05 cta_group::2): 256x256 output tile
+// per cluster of two CTAs.
+//
+// CTA r of the pair stages rows [128r, 128r+128) of the A tile and rows
+// [128r, 128r+128) of the B (weight) tile: each SM decodes and stores only half
+// of the weight tile, and the pair's tensor cores read each half once.  The
+// leader CTA (rank 0) issues tcgen05.mma.cta_group::2 (M=256, N=256, K=16) from
+// one thread; each CTA's tensor memory receives its own 128 accumulator rows.
+//
+// Synchronisation (all barriers sit at the same shared-memory offset in both
+// CTAs):
+//   full[s]    own CTA: its TMA loads (A half, packed weight half or BF16 half)
+//   ready[s]   leader only: both CTAs' stage s is ready for the MMA -- one
+//              arrival per decode warp of both CTAs (fused mode) or one per CTA
+//              from a bridge thread that watched full[s] (safe mode)
+//   empty[s]   both: MMAs reading stage s finished (multicast tcgen05.commit)
+//   tfull[a]   both: accumulator a complete (multicast tcgen05.commit)
+//   tempty[a]  leader only: both CTAs' epilogues drained accumulator a
+// No TMA multicast is used: each CTA loads only its own half.
+#pragma once
+
+#include "gemm.cuh"
+
+namespace mx {
+
+constexpr int kP2BM = 256, kP2BN = 256, kP2BK = 64;  // pair tile
+constexpr int kP2HalfRows = 128;
+constexpr int kP2ABytes = kP2HalfRows * kP2BK * 2;    // 16 KB
+constexpr int kP2BBytes = kP2HalfRows * kP2BK * 2;    // 16 KB
+constexpr int kP2PBytes = kP2HalfRows * kP2BK / 2;    // 4 KB
+
+template <int BMODE, int DECODE_WARPS>
+struct Pair2Cfg {
+  static constexpr int kStages = 6;
+  static constexpr int kDecodeWarps = BMODE == B_DECODE ? DECODE_WARPS : 0;
+  static constexpr int kThreads = 256 + 32 * kDecodeWarps;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + kStages * kP2ABytes;
+  static constexpr int kOffP = kOffB + kStages * kP2BBytes;
+  static constexpr int kOffBar = kOffP + (BMODE == B_DECODE ? kStages * kP2PBytes : 0);
+  // full, ready, empty per stage; tfull[2], tempty[2], drain
+  static constexpr int kNumBars = 3 * kStages + 5;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same shared variable in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
+  return d;
+}
+// Arrive on a barrier given by its shared::cluster address (possibly in the
+// peer CTA).  Default (.release.cta) semantics: a decoder orders its shared
+// stores for the tensor cores with fence.proxy.async before arriving, which is
+// what the MMA needs; a cluster-scope release here costs about 2x throughput.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort_flag = 1;
+      record_error(MXFP4_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma2_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the barrier at `bar`'s offset in every CTA of `mask` when all earlier
+// tcgen05 operations of this thread complete.
+__device__ __forceinline__ void umma2_commit_mc(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+struct DenseParams {
+  int M, N, K;
+  int num_m_blocks, num_n_blocks;  // in 256-row / 256-column pair tiles
+  const uint8_t* w_scales;
+  int64_t lds;
+  void* out;
+  int64_t ldo;
+  int out_dtype;
+  const void* bias;
+  int vec_ok;
+};
+
+template <int BMODE, int DECODE_WARPS, bool FP16>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECODE_WARPS>::kThreads, 1)
+    mxfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                           const DenseParams p) {
+  using Cfg = Pair2Cfg<BMODE, DECODE_WARPS>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* ready = bars + S;
+  uint64_t* empty = bars + 2 * S;
+  uint64_t* tfull = bars + 3 * S;
+  uint64_t* tempty = bars + 3 * S + 2;
+  uint64_t* drain = bars + 3 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int KT = p.K / kP2BK;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], BMODE == B_DECODE ? 2 * DECODE_WARPS : 2);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc2(tmem_slot, kTmemCols);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      int it = 0;
+      uint32_t armed = 0, armed_par = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        const int m_blk = t % p.num_m_blocks, n_blk = t / p.num_m_blocks;
+        const int arow = m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows;
+        const int brow = n_blk * kP2BN + static_cast<int>(rank) * kP2HalfRows;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait_cluster(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], kP2ABytes + (BMODE == B_DECODE ? kP2PBytes : kP2BBytes));
+          armed |= 1u << s;
+          armed_par = (armed_par & ~(1u << s)) | (ph << s);
+          tma_load_2d(smem + Cfg::kOffA + s * kP2ABytes, &tmap_a, &full[s], kt * kP2BK, arow);
+          if (BMODE == B_DECODE)
+            tma_load_2d_hint(smem + Cfg::kOffP + s * kP2PBytes, &tmap_b, &full[s], kt * (kP2BK / 2), brow, pol_w);
+          else
+            tma_load_2d_hint(smem + Cfg::kOffB + s * kP2BBytes, &tmap_b, &full[s], kt * kP2BK, brow, pol_w);
+        }
+      }
+      if (!ok || *abort_flag)
+        for (int s = 0; s < S; ++s)
+          if (armed & (1u << s)) mbar_drain(&full[s], (armed_par >> s) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(FP16 ? 0 : 1, kP2BM, kP2BN);
+      int it = 0, tl = 0;
+      bool ok = true, issued = false;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++tl) {
+        const int acc = tl & 1;
+        if (!mbar_wait_cluster(&tempty[acc], ((tl >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kAccCols;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait_cluster(&ready[s], ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = desc_sw128(smem_u32(smem + Cfg::kOffA + s * kP2ABytes));
+          const uint64_t bdesc = desc_sw128(smem_u32(smem + Cfg::kOffB + s * kP2BBytes));
+#pragma unroll
+          for (int k = 0; k < kP2BK / 16; ++k) umma2_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) != 0);
+          umma2_commit_mc(&empty[s], 0x3);
+          issued = true;
+        }
+        if (!ok) break;
+        umma2_commit_mc(&tfull[acc], 0x3);
+      }
+      if (!ok && issued) {
+        umma2_commit_mc(drain, 0x1);
+        mbar_drain(drain, 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2 && BMODE == B_TMA) {
+    // ------------------------------------------------------------------ bridge (safe mode)
+    if (lane == 0) {
+      const uint32_t ready_leader = mapa_shared(smem_u32(ready), 0);
+      int it = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters)
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_cluster(ready_leader + s * 8);
+        }
+    }
+    __syncwarp();
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int r_local = q * 32 + lane;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+    const int esz = out_esize(p.out_dtype);
+    int tl = 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters, ++tl) {
+      const int m_blk = t % p.num_m_blocks, n_blk = t / p.num_m_blocks;
+      const int acc = tl & 1;
+      if (!mbar_wait_cluster(&tfull[acc], (tl >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
+      const int row = m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows + r_local;
+      const bool row_ok = row < p.M;
+      uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(row_ok ? row : 0) * p.ldo * esz;
+#pragma unroll 1
+      for (int cc = 0; cc < kP2BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + cc * 32, r);
+        tmem_ld_wait();
+        const int col0 = n_blk * kP2BN + cc * 32;
+        if (row_ok && col0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          if (p.bias != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = col0 + i < p.N ? col0 + i : p.N - 1;
+              v[i] = round_to(round_to(v[i], p.out_dtype) + load_weight(p.bias, p.out_dtype, col), p.out_dtype);
+            }
+          }
+          store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------------ decoders (both CTAs)
+    if constexpr (BMODE == B_DECODE) {
+    constexpr int kThreadsPerRow = (DECODE_WARPS * 32) / kP2HalfRows;  // 2 or 4
+    constexpr int kChunks = 8 / kThreadsPerRow;                         // 16-byte output chunks per thread
+    const int d = threadIdx.x - 256;
+    const int r = d / kThreadsPerRow;                  // weight row in this CTA's half
+    const int part = d % kThreadsPerRow;
+    const int j0 = part * kChunks;                     // first chunk (8 K values each)
+    const int blk_in_tile = j0 / 4;                    // scale block (32 K) of this part within the 64-K stage
+    const uint32_t ready_leader = mapa_shared(smem_u32(ready), 0);
+    int it = 0;
+    bool ok = true;
+    for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+      const int n_blk = t / p.num_m_blocks;
+      const int grow = n_blk * kP2BN + static_cast<int>(rank) * kP2HalfRows + r;
+      const bool valid = grow < p.N;
+      const uint8_t* srow = p.w_scales + (valid ? static_cast<int64_t>(grow) * p.lds : 0);
+      uint32_t nxt = valid ? ldg_nc_u32(srow) : 0x7F7F7F7Fu;
+      uint32_t cur = 0;
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        if ((kt & 1) == 0) {
+          cur = nxt;
+          if (valid && kt + 2 < KT) nxt = ldg_nc_u32(srow + 4 * ((kt >> 1) + 1));
+        }
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+        const uint32_t code = (cur >> (8 * ((kt & 1) * 2 + blk_in_tile))) & 0xFF;
+        const uint32_t psrc = smem_u32(smem + Cfg::kOffP + s * kP2PBytes) + r * 32 + j0 * 4;
+        const uint32_t bdst = smem_u32(smem + Cfg::kOffB + s * kP2BBytes) + r * 128;
+        const uint32_t sw = r & 7;
+        uint32_t w[kChunks];
+        if constexpr (kChunks == 4) {
+          const uint4 q4 = ld_shared_v4(psrc);
+          w[0] = q4.x;
+          w[1] = q4.y;
+          w[2] = q4.z;
+          w[3] = q4.w;
+        } else {
+          asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(psrc));
+        }
+        if (FP16) {
+          const float f = e8m0_to_f32(code);
+#pragma unroll
+          for (int i = 0; i < kChunks; ++i) st_shared_v4(bdst + (((j0 + i) ^ sw) << 4), decode8_f16(w[i], f));
+        } else {
+          const uint32_t b = e8m0_to_bf16x2(code);
+#pragma unroll
+          for (int i = 0; i < kChunks; ++i) st_shared_v4(bdst + (((j0 + i) ^ sw) << 4), decode8_bf16(w[i], b));
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(ready_leader + s * 8);
+      }
+    }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's TMEM and barriers stay alive until the leader is done
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc2(tmem_base, kTmemCols);
+}
+
+}  // namespace mx
