@@ -159,11 +159,11 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const DenseParams&
   return MXFP4_OK;
 }
 
-// Decode warps per CTA of the fused pair kernel (8 or 16); MXFP4_B200_DECODE_WARPS overrides.
+// Decode warps per CTA of the fused pair kernel (8 or 16, default 8); MXFP4_B200_DECODE_WARPS overrides.
 int decode_warps() {
   static int v = [] {
     const char* e = std::getenv("MXFP4_B200_DECODE_WARPS");
-    return (e && std::atoi(e) == 8) ? 8 : 16;
+    return (e && std::atoi(e) == 16) ? 16 : 8;
   }();
   return v;
 }
@@ -377,7 +377,26 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   p.N = static_cast<int>(n);
   p.K = static_cast<int>(k);
   p.num_m_blocks = static_cast<int>((m + kP2BM - 1) / kP2BM);
-  p.num_n_blocks = static_cast<int>((n + kP2BN - 1) / kP2BN);
+  // pair tile width: the multiple of 32 (<= 256) that minimises rounds x width,
+  // so the last round of persistent clusters is not mostly idle
+  {
+    const int64_t clusters_max = std::max(1, info.sms / 2);
+    int best_bn = 256;
+    int64_t best_cost = -1;
+    for (int bn = 256; bn >= 128; bn -= 32) {
+      const int64_t tiles_bn = p.num_m_blocks * ((n + bn - 1) / bn);
+      const int64_t rounds = (tiles_bn + clusters_max - 1) / clusters_max;
+      const int64_t cost = rounds * (bn + 64);  // + fixed per-tile cost of a narrower tile
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best_bn = bn;
+      }
+    }
+    p.bn = best_bn;
+  }
+  p.num_n_blocks = static_cast<int>((n + p.bn - 1) / p.bn);
+  p.w_packed = static_cast<const uint8_t*>(w_packed);
+  p.ldw = ldw;
   p.w_scales = static_cast<const uint8_t*>(w_scales);
   p.lds = lds;
   p.out = out;
@@ -390,7 +409,7 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
 
   if (mode == MXFP4_LINEAR_FUSED) {
     if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kP2BK / 2,
-                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+                             p.bn / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
     if (decode_warps() == 8) {
       if (fp16) return launch_pair<B_DECODE, 8, true>(ta, tb, p, clusters, s);
@@ -405,7 +424,7 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
     return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
   MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
   if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
-  if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kP2BK, p.bn / 2, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   if (fp16) return launch_pair<B_TMA, 0, true>(ta, tb, p, clusters, s);
   return launch_pair<B_TMA, 0, false>(ta, tb, p, clusters, s);

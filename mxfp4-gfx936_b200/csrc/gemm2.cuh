@@ -119,8 +119,11 @@ __device__ __forceinline__ void umma2_commit_mc(uint64_t* bar, uint16_t mask) {
 }
 
 struct DenseParams {
+  const uint8_t* w_packed;         // unused by the kernels (TMA reads the packed weights)
+  int64_t ldw;
   int M, N, K;
-  int num_m_blocks, num_n_blocks;  // in 256-row / 256-column pair tiles
+  int bn;                          // pair tile width: multiple of 32, <= 256 (each CTA holds bn/2 weight rows)
+  int num_m_blocks, num_n_blocks;  // in 256-row / bn-column pair tiles
   const uint8_t* w_scales;
   int64_t lds;
   void* out;
@@ -194,12 +197,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
         const int m_blk = t % p.num_m_blocks, n_blk = t / p.num_m_blocks;
         const int arow = m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows;
-        const int brow = n_blk * kP2BN + static_cast<int>(rank) * kP2HalfRows;
+        const int brow = n_blk * p.bn + static_cast<int>(rank) * (p.bn / 2);
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait_cluster(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], kP2ABytes + (BMODE == B_DECODE ? kP2PBytes : kP2BBytes));
+          mbar_arrive_expect_tx(&full[s], kP2ABytes + (p.bn / 2) * (BMODE == B_DECODE ? kP2BK / 2 : kP2BK * 2));
           armed |= 1u << s;
           armed_par = (armed_par & ~(1u << s)) | (ph << s);
           tma_load_2d(smem + Cfg::kOffA + s * kP2ABytes, &tmap_a, &full[s], kt * kP2BK, arow);
@@ -217,7 +220,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(FP16 ? 0 : 1, kP2BM, kP2BN);
+      const uint32_t idesc = idesc_f16(FP16 ? 0 : 1, kP2BM, p.bn);
       int it = 0, tl = 0;
       bool ok = true, issued = false;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++tl) {
@@ -277,11 +280,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
       const bool row_ok = row < p.M;
       uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(row_ok ? row : 0) * p.ldo * esz;
 #pragma unroll 1
-      for (int cc = 0; cc < kP2BN / 32; ++cc) {
+      for (int cc = 0; cc < p.bn / 32; ++cc) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tbase + cc * 32, r);
         tmem_ld_wait();
-        const int col0 = n_blk * kP2BN + cc * 32;
+        const int col0 = n_blk * p.bn + cc * 32;
         if (row_ok && col0 < p.N) {
           float v[32];
 #pragma unroll
@@ -313,21 +316,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
     const uint32_t ready_leader = mapa_shared(smem_u32(ready), 0);
     int it = 0;
     bool ok = true;
+    const bool row_live = r < p.bn / 2;
     for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
       const int n_blk = t / p.num_m_blocks;
-      const int grow = n_blk * kP2BN + static_cast<int>(rank) * kP2HalfRows + r;
-      const bool valid = grow < p.N;
+      const int grow = n_blk * p.bn + static_cast<int>(rank) * (p.bn / 2) + r;
+      const bool valid = row_live && grow < p.N;
       const uint8_t* srow = p.w_scales + (valid ? static_cast<int64_t>(grow) * p.lds : 0);
-      uint32_t nxt = valid ? ldg_nc_u32(srow) : 0x7F7F7F7Fu;
+      // one 32-bit scale word covers two 64-K stages; keep two words in flight
+      const int nwords = KT / 2;
+      uint32_t w0 = valid ? ldg_nc_u32(srow) : 0x7F7F7F7Fu;
+      uint32_t w1 = (valid && nwords > 1) ? ldg_nc_u32(srow + 4) : 0x7F7F7F7Fu;
       uint32_t cur = 0;
       for (int kt = 0; kt < KT; ++kt, ++it) {
         if ((kt & 1) == 0) {
-          cur = nxt;
-          if (valid && kt + 2 < KT) nxt = ldg_nc_u32(srow + 4 * ((kt >> 1) + 1));
+          cur = w0;
+          w0 = w1;
+          const int nw = (kt >> 1) + 2;
+          if (valid && nw < nwords) w1 = ldg_nc_u32(srow + 4 * nw);
         }
         const int s = it % S;
         const uint32_t ph = (it / S) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+        if (!row_live) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(ready_leader + s * 8);
+          continue;
+        }
         const uint32_t code = (cur >> (8 * ((kt & 1) * 2 + blk_in_tile))) & 0xFF;
         const uint32_t psrc = smem_u32(smem + Cfg::kOffP + s * kP2PBytes) + r * 32 + j0 * 4;
         const uint32_t bdst = smem_u32(smem + Cfg::kOffB + s * kP2BBytes) + r * 128;
