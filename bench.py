@@ -353,6 +353,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the non-headline configurations")
+    ap.add_argument("--workload", default=None, choices=["oproj", "safe", "decode", "moe", "w4a4"],
+                    help="run only this configuration (for profiling); prints its timing as JSON")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -368,6 +370,8 @@ def main():
 
     if world > 1:
         return run_sharded(args, soft, world, rank, device, pk, pk_kind)
+    if args.workload is not None:
+        return run_one(args, soft, device)
 
     sampler = ClockSampler(local)
     ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "fused", device, sampler=sampler)
@@ -425,6 +429,23 @@ def main():
     if status:
         line["device_status"] = status
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_one(args, soft, device):
+    """One configuration on its own (profiling aid; not the driver's line)."""
+    w = args.workload
+    if w == "oproj":
+        ms = bench_linear(soft, OPROJ, args.steps, args.warmup, 4, "fused", device, seed0=10)
+    elif w == "safe":
+        ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "safe", device, seed0=20)
+    elif w == "decode":
+        ms = bench_linear(soft, (1, QKV[1], QKV[2]), args.steps, args.warmup, 32, "fused", device, seed0=101)
+    elif w == "moe":
+        ms = bench_moe(soft, args.steps, args.warmup, device)
+    else:
+        ms = bench_w4a4(soft, args.steps, args.warmup, device)
+    print(json.dumps({"workload": w, "ms_per_step": ms, "steps": args.steps}), flush=True)
     return 0
 
 

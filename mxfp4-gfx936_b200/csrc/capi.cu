@@ -143,11 +143,11 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
   return MXFP4_OK;
 }
 
-template <int BMODE, int DW, bool FP16>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const DenseParams& p, int clusters,
+template <int AMODE, int BMODE, int EPI, bool FP16, int DW>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& p, int clusters,
                 cudaStream_t stream) {
   using Cfg = Pair2Cfg<BMODE, DW>;
-  auto kern = mxfp4_gemm_pair_kernel<BMODE, DW, FP16>;
+  auto kern = mxfp4_gemm_pair_kernel<AMODE, BMODE, EPI, FP16, DW>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -157,6 +157,16 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const DenseParams&
   kern<<<2 * clusters, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
+}
+
+// Routed GEMM on CTA pairs over 256-route blocks (fused decode, 8 decode warps).
+template <int AMODE, int EPI>
+int routed_pair_gemm(bool fp16, const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& p, int sms,
+                     cudaStream_t stream) {
+  const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
+  const int clusters = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms / 2)));
+  if (fp16) return launch_pair<AMODE, B_DECODE, EPI, true, 8>(ta, tb, p, clusters, stream);
+  return launch_pair<AMODE, B_DECODE, EPI, false, 8>(ta, tb, p, clusters, stream);
 }
 
 // Decode warps per CTA of the fused pair kernel (8 or 16, default 8); MXFP4_B200_DECODE_WARPS overrides.
@@ -233,16 +243,6 @@ int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_expert
         sorted_ids);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
-}
-
-// Launch a grouped GEMM over routed blocks (block size kBM).
-template <int AMODE, int EPI>
-int grouped_gemm(bool fp16, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                 int sms, cudaStream_t stream) {
-  const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms)));
-  if (fp16) return launch_gemm<AMODE, B_DECODE, EPI, true>(ta, tb, p, grid, stream);
-  return launch_gemm<AMODE, B_DECODE, EPI, false>(ta, tb, p, grid, stream);
 }
 
 }  // namespace
@@ -372,7 +372,7 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   CUtensorMap ta, tb;
   if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
 
-  DenseParams p{};
+  PairParams p{};
   p.M = static_cast<int>(m);
   p.N = static_cast<int>(n);
   p.K = static_cast<int>(k);
@@ -395,9 +395,8 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
     p.bn = best_bn;
   }
   p.num_n_blocks = static_cast<int>((n + p.bn - 1) / p.bn);
-  p.w_packed = static_cast<const uint8_t*>(w_packed);
-  p.ldw = ldw;
   p.w_scales = static_cast<const uint8_t*>(w_scales);
+  p.w_rows_per_expert = n;
   p.lds = lds;
   p.out = out;
   p.ldo = ldo;
@@ -411,12 +410,12 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
     if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kP2BK / 2,
                              p.bn / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
-    if (decode_warps() == 8) {
-      if (fp16) return launch_pair<B_DECODE, 8, true>(ta, tb, p, clusters, s);
-      return launch_pair<B_DECODE, 8, false>(ta, tb, p, clusters, s);
+    if (decode_warps() == 16) {
+      if (fp16) return launch_pair<A_TMA, B_DECODE, EPI_DENSE, true, 16>(ta, tb, p, clusters, s);
+      return launch_pair<A_TMA, B_DECODE, EPI_DENSE, false, 16>(ta, tb, p, clusters, s);
     }
-    if (fp16) return launch_pair<B_DECODE, 16, true>(ta, tb, p, clusters, s);
-    return launch_pair<B_DECODE, 16, false>(ta, tb, p, clusters, s);
+    if (fp16) return launch_pair<A_TMA, B_DECODE, EPI_DENSE, true, 8>(ta, tb, p, clusters, s);
+    return launch_pair<A_TMA, B_DECODE, EPI_DENSE, false, 8>(ta, tb, p, clusters, s);
   }
   // safe: explicit dequant of W into the workspace, then the same MMA pipeline
   const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
@@ -426,8 +425,8 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
   if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kP2BK, p.bn / 2, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if (fp16) return launch_pair<B_TMA, 0, true>(ta, tb, p, clusters, s);
-  return launch_pair<B_TMA, 0, false>(ta, tb, p, clusters, s);
+  if (fp16) return launch_pair<A_TMA, B_TMA, EPI_DENSE, true, 0>(ta, tb, p, clusters, s);
+  return launch_pair<A_TMA, B_TMA, EPI_DENSE, false, 0>(ta, tb, p, clusters, s);
 }
 
 int64_t mxfp4_moe_route_capacity(int64_t num_routes, int num_experts, int block_m) {
@@ -466,10 +465,10 @@ size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_exp
                                       int64_t k, int a_dtype, int c_dtype) {
   (void)n;
   const int64_t routes = num_tokens * top_k;
-  const int64_t cap = route_capacity(routes, num_experts, kBM);
+  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
   size_t b = 0;
   b += align_up(sizeof(int32_t) * cap, 256);
-  b += align_up(sizeof(int32_t) * (cap / kBM + 1), 256);
+  b += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
   b += 256;  // num_post_padded
   b += route_ws_bytes(routes, num_experts);
   const int cdt = c_dtype == MXFP4_DTYPE_F32 ? a_dtype : c_dtype;
@@ -517,11 +516,11 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   MX_CUDA(cudaMemsetAsync(C, 0, static_cast<size_t>(routes) * n * esz, s));
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  const int64_t cap = route_capacity(routes, num_experts, kBM);
+  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
   int32_t* sorted_ids = reinterpret_cast<int32_t*>(ws);
   ws += align_up(sizeof(int32_t) * cap, 256);
   int32_t* block_expert = reinterpret_cast<int32_t*>(ws);
-  ws += align_up(sizeof(int32_t) * (cap / kBM + 1), 256);
+  ws += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
   int32_t* post = reinterpret_cast<int32_t*>(ws);
   ws += 256;
   uint8_t* route_ws = ws;
@@ -537,23 +536,23 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
     MX_CUDA(cudaGetLastError());
     a_eff = ws;
   }
-  if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kBM, sorted_ids, block_expert, post,
-                         cap, route_ws, s))
+  if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kP2BM, sorted_ids, block_expert, post, cap,
+                         route_ws, s))
     return rc;
 
   CUtensorMap ta{}, tb;
   if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, static_cast<uint64_t>(num_experts) * n,
-                           k / 2, kBK / 2, kBN / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
+                           k / 2, kP2BK / 2, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
   MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
-  GemmParams p{};
+  PairParams p{};
   p.N = static_cast<int>(n);
   p.K = static_cast<int>(k);
-  p.num_m_blocks = static_cast<int>(cap / kBM);
-  p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
+  p.bn = 256;
+  p.num_m_blocks = static_cast<int>(cap / kP2BM);
+  p.num_n_blocks = static_cast<int>((n + p.bn - 1) / p.bn);
   p.a_ptr = static_cast<const uint8_t*>(a_eff);
   p.lda = k;
-  p.a_rows = static_cast<int>(num_tokens);
   p.w_scales = static_cast<const uint8_t*>(B_mx_scale);
   p.lds = k / 32;
   p.w_rows_per_expert = n;
@@ -572,7 +571,7 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   p.c_stride_t = static_cast<int64_t>(top_k) * n;
   p.c_stride_j = n;
   p.vec_ok = aligned(C, 16) && (n * esz) % 16 == 0;
-  return grouped_gemm<A_GATHER, EPI_MOE>(cdt == MXFP4_DTYPE_F16, ta, tb, p, info.sms, s);
+  return routed_pair_gemm<A_GATHER, EPI_MOE>(cdt == MXFP4_DTYPE_F16, ta, tb, p, info.sms, s);
 }
 
 // Same operation as mxfp4_fused_moe, with its scratch taken from the static
@@ -694,10 +693,10 @@ int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const vo
 size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t hidden,
                                       int64_t inter) {
   const int64_t routes = num_tokens * top_k;
-  const int64_t cap = route_capacity(routes, num_experts, kBM);
+  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
   size_t b = 0;
   b += align_up(sizeof(int32_t) * cap, 256);
-  b += align_up(sizeof(int32_t) * (cap / kBM + 1), 256);
+  b += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
   b += 256;
   b += route_ws_bytes(routes, num_experts);
   b += align_up(static_cast<size_t>(cap) * inter * 2, 256);     // h in routed order
@@ -726,12 +725,12 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   cudaStream_t s = as_stream(stream);
   const int64_t routes = num_tokens * top_k;
   if (num_tokens == 0) return MXFP4_OK;
-  const int64_t cap = route_capacity(routes, num_experts, kBM);
+  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* sorted_ids = reinterpret_cast<int32_t*>(ws);
   ws += align_up(sizeof(int32_t) * cap, 256);
   int32_t* block_expert = reinterpret_cast<int32_t*>(ws);
-  ws += align_up(sizeof(int32_t) * (cap / kBM + 1), 256);
+  ws += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
   int32_t* post = reinterpret_cast<int32_t*>(ws);
   ws += 256;
   uint8_t* route_ws = ws;
@@ -740,7 +739,7 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
   void* ybuf = ws;
 
-  if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kBM, sorted_ids, block_expert, post, cap,
+  if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kP2BM, sorted_ids, block_expert, post, cap,
                          route_ws, s))
     return rc;
 
@@ -748,17 +747,17 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   {
     CUtensorMap ta{}, tb;
     if (int rc = make_map_2d(&tb, w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hidden / 2,
-                             static_cast<uint64_t>(num_experts) * 2 * inter, hidden / 2, kBK / 2, kBN / 2,
+                             static_cast<uint64_t>(num_experts) * 2 * inter, hidden / 2, kP2BK / 2, kP2HalfRows,
                              CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
-    GemmParams p{};
+    PairParams p{};
     p.N = static_cast<int>(2 * inter);
     p.K = static_cast<int>(hidden);
-    p.num_m_blocks = static_cast<int>(cap / kBM);
-    p.num_n_blocks = static_cast<int>((inter + kBN / 2 - 1) / (kBN / 2));
+    p.bn = 256;
+    p.num_m_blocks = static_cast<int>(cap / kP2BM);
+    p.num_n_blocks = static_cast<int>((inter + p.bn / 2 - 1) / (p.bn / 2));
     p.a_ptr = static_cast<const uint8_t*>(x);
     p.lda = hidden;
-    p.a_rows = static_cast<int>(num_tokens);
     p.w_scales = static_cast<const uint8_t*>(w13_scale);
     p.lds = hidden / 32;
     p.w_rows_per_expert = 2 * inter;
@@ -772,23 +771,24 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
     p.ldo = inter;
     p.out_dtype = MXFP4_DTYPE_BF16;
     p.vec_ok = 1;
-    if (int rc = grouped_gemm<A_GATHER, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
+    if (int rc = routed_pair_gemm<A_GATHER, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
   }
   // down with route weights, scattered to y[route] = [routes, hidden]
   {
     CUtensorMap ta, tb;
-    if (int rc = make_map_2d(&ta, hbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inter, cap, inter * 2, kBK, kBM,
-                             CU_TENSOR_MAP_SWIZZLE_128B))
+    if (int rc = make_map_2d(&ta, hbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inter, cap, inter * 2, kP2BK,
+                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
     if (int rc = make_map_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inter / 2,
-                             static_cast<uint64_t>(num_experts) * hidden, inter / 2, kBK / 2, kBN / 2,
+                             static_cast<uint64_t>(num_experts) * hidden, inter / 2, kP2BK / 2, kP2HalfRows,
                              CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
-    GemmParams p{};
+    PairParams p{};
     p.N = static_cast<int>(hidden);
     p.K = static_cast<int>(inter);
-    p.num_m_blocks = static_cast<int>(cap / kBM);
-    p.num_n_blocks = static_cast<int>((hidden + kBN - 1) / kBN);
+    p.bn = 256;
+    p.num_m_blocks = static_cast<int>(cap / kP2BM);
+    p.num_n_blocks = static_cast<int>((hidden + p.bn - 1) / p.bn);
     p.w_scales = static_cast<const uint8_t*>(w2_scale);
     p.lds = inter / 32;
     p.w_rows_per_expert = hidden;
@@ -807,7 +807,7 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
     p.c_stride_t = hidden;
     p.c_stride_j = 0;
     p.vec_ok = 1;
-    if (int rc = grouped_gemm<A_TMA, EPI_MOE>(false, ta, tb, p, info.sms, s)) return rc;
+    if (int rc = routed_pair_gemm<A_TMA, EPI_MOE>(false, ta, tb, p, info.sms, s)) return rc;
   }
   const int64_t vecs = num_tokens * (hidden / 8);
   const int grid = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, int64_t(info.sms) * 8));

@@ -118,44 +118,82 @@ __global__ void __launch_bounds__(kRouteThreads) route_count_kernel(
   if (r < num_routes) rank_out[r] = e >= 0 ? warp_cnt[warp * num_experts + e] + rank_in_warp : -1;
 }
 
-// One CTA.  hist[c][e] -> chunk bases (in place); blk_off[e] = first block of e.
+// One CTA of 1024 threads.  hist[c][e] -> per-chunk bases (in place, exclusive
+// prefix over chunks per expert); blk_off[e] = first block of expert e
+// (exclusive scan of the padded block counts); writes the per-block expert ids,
+// the pad entries and the used length.  The histogram is staged through
+// shared memory in tiles of rows so every global access is coalesced.
 __global__ void __launch_bounds__(1024) route_offsets_kernel(
     int32_t* __restrict__ hist, int num_chunks, int num_experts, int block_m, int64_t num_routes,
     int32_t* __restrict__ blk_off, int32_t* __restrict__ sorted_ids,
     int32_t* __restrict__ block_expert, int32_t* __restrict__ num_post_padded,
     int64_t capacity_blocks) {
-  __shared__ int32_t nblk[kMaxExperts];
-  __shared__ int32_t scan[kMaxExperts];
+  constexpr int kTileElems = 8192;  // 32 KB of counts per tile
+  __shared__ int32_t tile[kTileElems];
   __shared__ int32_t total_s[kMaxExperts];
-  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
-    int run = 0;
-    for (int c = 0; c < num_chunks; ++c) {
-      const int64_t i = static_cast<int64_t>(c) * num_experts + e;
-      const int v = hist[i];
-      hist[i] = run;
-      run += v;
+  __shared__ int32_t scan_s[kMaxExperts];
+  __shared__ int32_t warp_sums[32];
+  const int rows_per_tile = kTileElems / num_experts > 0 ? kTileElems / num_experts : 1;
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) total_s[e] = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < num_chunks; c0 += rows_per_tile) {
+    const int rows = min(rows_per_tile, num_chunks - c0);
+    const int n = rows * num_experts;
+    int32_t* g = hist + static_cast<int64_t>(c0) * num_experts;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) tile[i] = g[i];
+    __syncthreads();
+    for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
+      int run = total_s[e];
+      for (int c = 0; c < rows; ++c) {
+        const int v = tile[c * num_experts + e];
+        tile[c * num_experts + e] = run;
+        run += v;
+      }
+      total_s[e] = run;
     }
-    total_s[e] = run;
-    nblk[e] = (run + block_m - 1) / block_m;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) g[i] = tile[i];
+    __syncthreads();
+  }
+  // exclusive scan of padded block counts over experts (E <= 1024: one per thread)
+  const int e = threadIdx.x;
+  const int nb = e < num_experts ? (total_s[e] + block_m - 1) / block_m : 0;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int incl = nb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_sums[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    int w = warp_sums[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_sums[lane] = w;  // inclusive over warps
   }
   __syncthreads();
-  if (threadIdx.x == 0) {  // E <= 1024: a serial scan is a few microseconds at most
-    int run = 0;
-    for (int e = 0; e < num_experts; ++e) {
-      scan[e] = run;
-      run += nblk[e];
-    }
-    num_post_padded[0] = run * block_m;
-    for (int64_t b = run; b < capacity_blocks; ++b) block_expert[b] = -1;
-  }
+  const int excl = incl - nb + (wid > 0 ? warp_sums[wid - 1] : 0);
+  if (e < num_experts) scan_s[e] = excl;
+  const int total_blocks = warp_sums[31];
+  if (threadIdx.x == 0) num_post_padded[0] = total_blocks * block_m;
+  for (int64_t b = total_blocks + threadIdx.x; b < capacity_blocks; b += blockDim.x) block_expert[b] = -1;
   __syncthreads();
   const int32_t pad = static_cast<int32_t>(num_routes);
-  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
-    blk_off[e] = scan[e];
-    for (int b = 0; b < nblk[e]; ++b) block_expert[scan[e] + b] = e;
-    const int64_t beg = static_cast<int64_t>(scan[e]) * block_m + total_s[e];
-    const int64_t end = static_cast<int64_t>(scan[e] + nblk[e]) * block_m;
-    for (int64_t i = beg; i < end; ++i) sorted_ids[i] = pad;
+  if (e < num_experts) {
+    blk_off[e] = excl;
+    for (int b = 0; b < nb; ++b) block_expert[excl + b] = e;
+  }
+  // pad entries of every expert's last block: spread over all threads
+  for (int x = 0; x < num_experts; ++x) {
+    const int beg_in = total_s[x];
+    const int end_in = ((beg_in + block_m - 1) / block_m) * block_m;
+    const int64_t base = static_cast<int64_t>(scan_s[x]) * block_m;
+    for (int i = beg_in + threadIdx.x; i < end_in; i += blockDim.x) sorted_ids[base + i] = pad;
   }
 }
 

@@ -1,5 +1,7 @@
-// Dense W4A16 linear on CTA pairs (tcgen05 cta_group::2): 256x256 output tile
-// per cluster of two CTAs.
+// W4A16 GEMMs on CTA pairs (tcgen05 cta_group::2): a 256-row x bn-column
+// output tile per cluster of two CTAs.  One template serves the dense linear
+// (fused and safe modes), the routed MoE op and both passes of the MoE layer
+// (256-row blocks of routes of one expert).
 //
 // CTA r of the pair stages rows [128r, 128r+128) of the A tile and rows
 // [128r, 128r+128) of the B (weight) tile: each SM decodes and stores only half
@@ -118,25 +120,89 @@ __device__ __forceinline__ void umma2_commit_mc(uint64_t* bar, uint16_t mask) {
       : "memory");
 }
 
-struct DenseParams {
-  const uint8_t* w_packed;         // unused by the kernels (TMA reads the packed weights)
-  int64_t ldw;
-  int M, N, K;
-  int bn;                          // pair tile width: multiple of 32, <= 256 (each CTA holds bn/2 weight rows)
-  int num_m_blocks, num_n_blocks;  // in 256-row / bn-column pair tiles
-  const uint8_t* w_scales;
+struct PairParams {
+  int M, N, K;                     // dense: rows of A; N: output columns (GLU: 2*inter); K: reduction
+  int bn;                          // tile width: multiple of 32, <= 256 (each CTA holds bn/2 weight rows)
+  int num_m_blocks, num_n_blocks;  // dense: ceil(M/256); routed: capacity blocks of 256 routes
+  // routed A gather (A_GATHER): row of route r is A[r / top_k]
+  const uint8_t* a_ptr;
+  int64_t lda;                     // elements
+  int a_row_offset;                // TMA row origin of A
+  // weights
+  const uint8_t* w_scales;         // [rows, K/32]
   int64_t lds;
+  int64_t w_rows_per_expert;       // N (plain) or 2*inter (GLU)
+  int glu_inter;
+  // routing
+  const int32_t* sorted_ids;
+  const int32_t* block_expert;
+  const int32_t* num_post_padded;
+  int num_routes;
+  int top_k;
+  // epilogue
   void* out;
-  int64_t ldo;
+  int64_t ldo;                     // elements (dense / GLU row stride)
   int out_dtype;
   const void* bias;
+  const float* a_scale;            // routed op: NULL means 1
+  const float* b_scale;
+  const void* topk_w;
+  int w_dtype;
+  int mul_w;
+  int64_t c_stride_t, c_stride_j;  // routed C row offset, elements
   int vec_ok;
 };
+using DenseParams = PairParams;
 
-template <int BMODE, int DECODE_WARPS, bool FP16>
+struct PairTile {
+  int m_blk, n_blk, expert;
+};
+
+template <int EPI>
+__device__ __forceinline__ PairTile pair_tile(const PairParams& p, int t, int nmb) {
+  PairTile c;
+  c.m_blk = t % nmb;
+  c.n_blk = t / nmb;
+  c.expert = EPI == EPI_DENSE ? 0 : p.block_expert[c.m_blk];
+  return c;
+}
+
+// Weight row of local B row r (0..bn/2-1) of this CTA.  GLU: CTA 0 holds the
+// gate rows and CTA 1 the up rows of the same bn/2 intermediate columns.
+template <int EPI>
+__device__ __forceinline__ int64_t pair_weight_row(const PairParams& p, const PairTile& c, uint32_t rank, int r,
+                                                   bool& valid) {
+  const int64_t base = static_cast<int64_t>(c.expert) * p.w_rows_per_expert;
+  if (EPI == EPI_GLU) {
+    const int col = c.n_blk * (p.bn / 2) + r;
+    valid = col < p.glu_inter;
+    return base + (rank == 0 ? col : p.glu_inter + col);
+  }
+  const int col = c.n_blk * p.bn + static_cast<int>(rank) * (p.bn / 2) + r;
+  valid = col < p.N;
+  return base + col;
+}
+
+// Rounding chain of the routed op for one 32-column chunk (soft:487-494),
+// compiled per output dtype so the element loop has no dtype branches.
+template <int OUT>
+__device__ __forceinline__ void moe_chunk(float (&v)[32], float asc, float bsc, float rw, bool scales, bool mul) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float x = round_to(v[i], OUT);
+    if (scales) {
+      x = round_to(x * asc, OUT);
+      x = round_to(x * bsc, OUT);
+    }
+    if (mul) x = round_to(x * rw, OUT);
+    v[i] = x;
+  }
+}
+
+template <int AMODE, int BMODE, int EPI, bool FP16, int DECODE_WARPS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECODE_WARPS>::kThreads, 1)
     mxfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                           const DenseParams p) {
+                           const PairParams p) {
   using Cfg = Pair2Cfg<BMODE, DECODE_WARPS>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -157,10 +223,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
   const int KT = p.K / kP2BK;
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
+  const int half_rows = p.bn / 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], AMODE == A_GATHER ? 33 : 1);
       mbar_init(&ready[s], BMODE == B_DECODE ? 2 * DECODE_WARPS : 2);
       mbar_init(&empty[s], 1);
     }
@@ -173,7 +240,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tmap_a);
+    if (AMODE == A_TMA) prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
   }
   if (warp == 1) {
@@ -185,34 +252,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
   cluster_sync();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+  int nmb = p.num_m_blocks;
+  if (EPI != EPI_DENSE) {
+    const int used = p.num_post_padded[0] / kP2BM;
+    nmb = used < nmb ? used : nmb;
+  }
+  const int num_tiles = nmb * p.num_n_blocks;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer (both CTAs)
-    if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
-      int it = 0;
-      uint32_t armed = 0, armed_par = 0;
-      bool ok = true;
-      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
-        const int m_blk = t % p.num_m_blocks, n_blk = t / p.num_m_blocks;
-        const int arow = m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows;
-        const int brow = n_blk * p.bn + static_cast<int>(rank) * (p.bn / 2);
-        for (int kt = 0; kt < KT; ++kt, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (it / S) & 1;
+    // lane 0 issues the TMA loads; in gather mode all 32 lanes copy A rows
+    const uint64_t pol_w = policy_evict_first();
+    int it = 0;
+    uint32_t armed = 0, armed_par = 0;
+    bool ok = true;
+    if (AMODE == A_GATHER || lane == 0)
+    for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+      const PairTile c = pair_tile<EPI>(p, t, nmb);
+      bool v0;
+      const int brow = static_cast<int>(pair_weight_row<EPI>(p, c, rank, 0, v0));
+      const int arow = p.a_row_offset + c.m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows;
+      const uint8_t* gsrc[4];
+      uint32_t gbytes[4];
+      if (AMODE == A_GATHER) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = lane + 32 * i;
+          const int route = p.sorted_ids[c.m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows + r];
+          const int src_row = route < p.num_routes ? route / p.top_k : -1;
+          gsrc[i] = p.a_ptr + (src_row >= 0 ? static_cast<int64_t>(src_row) * p.lda * 2 : 0);
+          gbytes[i] = src_row >= 0 ? 16u : 0u;
+        }
+      }
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1;
+        if (AMODE == A_GATHER || lane == 0) {
           if (!mbar_wait_cluster(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], kP2ABytes + (p.bn / 2) * (BMODE == B_DECODE ? kP2BK / 2 : kP2BK * 2));
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], (AMODE == A_TMA ? kP2ABytes : 0) +
+                                              half_rows * (BMODE == B_DECODE ? kP2BK / 2 : kP2BK * 2));
           armed |= 1u << s;
           armed_par = (armed_par & ~(1u << s)) | (ph << s);
-          tma_load_2d(smem + Cfg::kOffA + s * kP2ABytes, &tmap_a, &full[s], kt * kP2BK, arow);
+          if (AMODE == A_TMA) tma_load_2d(smem + Cfg::kOffA + s * kP2ABytes, &tmap_a, &full[s], kt * kP2BK, arow);
           if (BMODE == B_DECODE)
             tma_load_2d_hint(smem + Cfg::kOffP + s * kP2PBytes, &tmap_b, &full[s], kt * (kP2BK / 2), brow, pol_w);
           else
             tma_load_2d_hint(smem + Cfg::kOffB + s * kP2BBytes, &tmap_b, &full[s], kt * kP2BK, brow, pol_w);
         }
+        if (AMODE == A_GATHER) {
+          const uint32_t abase = smem_u32(smem + Cfg::kOffA + s * kP2ABytes);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = lane + 32 * i;
+            const uint8_t* src = gsrc[i] + static_cast<int64_t>(kt) * kP2BK * 2;
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) cp_async_16(abase + r * 128 + ((ch ^ (r & 7)) << 4), src + ch * 16, gbytes[i]);
+          }
+          cp_async_arrive_noinc(&full[s]);
+        }
       }
-      if (!ok || *abort_flag)
+      if (AMODE == A_GATHER) __syncwarp();
+    }
+    if (!ok || *abort_flag) {
+      if (AMODE == A_GATHER) cp_async_wait_all();
+      if (lane == 0)
         for (int s = 0; s < S; ++s)
           if (armed & (1u << s)) mbar_drain(&full[s], (armed_par >> s) & 1u);
     }
@@ -271,32 +376,84 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
     const int esz = out_esize(p.out_dtype);
     int tl = 0;
     for (int t = cluster_id; t < num_tiles; t += num_clusters, ++tl) {
-      const int m_blk = t % p.num_m_blocks, n_blk = t / p.num_m_blocks;
+      const PairTile c = pair_tile<EPI>(p, t, nmb);
       const int acc = tl & 1;
       if (!mbar_wait_cluster(&tfull[acc], (tl >> 1) & 1, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
-      const int row = m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows + r_local;
-      const bool row_ok = row < p.M;
-      uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(row_ok ? row : 0) * p.ldo * esz;
+      const int pos = c.m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows + r_local;  // row of the block
+      if (EPI == EPI_DENSE) {
+        const bool row_ok = pos < p.M;
+        uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(row_ok ? pos : 0) * p.ldo * esz;
 #pragma unroll 1
-      for (int cc = 0; cc < p.bn / 32; ++cc) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + cc * 32, r);
-        tmem_ld_wait();
-        const int col0 = n_blk * p.bn + cc * 32;
-        if (row_ok && col0 < p.N) {
-          float v[32];
+        for (int cc = 0; cc < p.bn / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + cc * 32, r);
+          tmem_ld_wait();
+          const int col0 = c.n_blk * p.bn + cc * 32;
+          if (row_ok && col0 < p.N) {
+            float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          if (p.bias != nullptr) {
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            if (p.bias != nullptr) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int col = col0 + i < p.N ? col0 + i : p.N - 1;
+                v[i] = round_to(round_to(v[i], p.out_dtype) + load_weight(p.bias, p.out_dtype, col), p.out_dtype);
+              }
+            }
+            store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
+          }
+        }
+      } else if (EPI == EPI_MOE) {
+        const int route = p.sorted_ids[pos];
+        const bool row_ok = route < p.num_routes;
+        const bool scales = p.a_scale != nullptr;
+        const float asc = scales ? p.a_scale[0] : 1.0f;
+        const float bsc = scales ? p.b_scale[c.expert] : 1.0f;
+        const bool mul = p.mul_w != 0;
+        const float rw = (row_ok && mul) ? load_weight(p.topk_w, p.w_dtype, route) : 1.0f;
+        const int64_t roff = row_ok ? (static_cast<int64_t>(route / p.top_k) * p.c_stride_t +
+                                       static_cast<int64_t>(route % p.top_k) * p.c_stride_j)
+                                    : 0;
+        uint8_t* orow = static_cast<uint8_t*>(p.out) + roff * esz;
+#pragma unroll 1
+        for (int cc = 0; cc < p.bn / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + cc * 32, r);
+          tmem_ld_wait();
+          const int col0 = c.n_blk * p.bn + cc * 32;
+          if (row_ok && col0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            if (p.out_dtype == MXFP4_DTYPE_BF16) moe_chunk<MXFP4_DTYPE_BF16>(v, asc, bsc, rw, scales, mul);
+            else if (p.out_dtype == MXFP4_DTYPE_F16) moe_chunk<MXFP4_DTYPE_F16>(v, asc, bsc, rw, scales, mul);
+            else moe_chunk<MXFP4_DTYPE_F32>(v, asc, bsc, rw, scales, mul);
+            store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
+          }
+        }
+      } else {  // EPI_GLU: h = bf16(bf16(silu(bf16 g)) * bf16 u), written in routed order
+        uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(pos) * p.ldo * 2;
+#pragma unroll 1
+        for (int cc = 0; cc < p.bn / 64; ++cc) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(tbase + cc * 32, g);
+          tmem_ld_32x32b_x32(tbase + p.bn / 2 + cc * 32, u);
+          tmem_ld_wait();
+          const int col0 = c.n_blk * (p.bn / 2) + cc * 32;
+          if (col0 < p.glu_inter) {
+            float v[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const int col = col0 + i < p.N ? col0 + i : p.N - 1;
-              v[i] = round_to(round_to(v[i], p.out_dtype) + load_weight(p.bias, p.out_dtype, col), p.out_dtype);
+              const float gg = round_bf16(__uint_as_float(g[i]));
+              const float uu = round_bf16(__uint_as_float(u[i]));
+              const float sg = round_bf16(gg / (1.0f + expf(-gg)));
+              v[i] = round_bf16(sg * uu);
             }
+            store_row32(orow + static_cast<int64_t>(col0) * 2, MXFP4_DTYPE_BF16, v, p.glu_inter - col0,
+                        p.vec_ok != 0);
           }
-          store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
         }
       }
       tc_fence_before();
@@ -306,70 +463,68 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
   } else if (warp >= 8) {
     // ------------------------------------------------------------------ decoders (both CTAs)
     if constexpr (BMODE == B_DECODE) {
-    constexpr int kThreadsPerRow = (DECODE_WARPS * 32) / kP2HalfRows;  // 2 or 4
-    constexpr int kChunks = 8 / kThreadsPerRow;                         // 16-byte output chunks per thread
-    const int d = threadIdx.x - 256;
-    const int r = d / kThreadsPerRow;                  // weight row in this CTA's half
-    const int part = d % kThreadsPerRow;
-    const int j0 = part * kChunks;                     // first chunk (8 K values each)
-    const int blk_in_tile = j0 / 4;                    // scale block (32 K) of this part within the 64-K stage
-    const uint32_t ready_leader = mapa_shared(smem_u32(ready), 0);
-    int it = 0;
-    bool ok = true;
-    const bool row_live = r < p.bn / 2;
-    for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
-      const int n_blk = t / p.num_m_blocks;
-      const int grow = n_blk * p.bn + static_cast<int>(rank) * (p.bn / 2) + r;
-      const bool valid = row_live && grow < p.N;
-      const uint8_t* srow = p.w_scales + (valid ? static_cast<int64_t>(grow) * p.lds : 0);
-      // one 32-bit scale word covers two 64-K stages; keep two words in flight
-      const int nwords = KT / 2;
-      uint32_t w0 = valid ? ldg_nc_u32(srow) : 0x7F7F7F7Fu;
-      uint32_t w1 = (valid && nwords > 1) ? ldg_nc_u32(srow + 4) : 0x7F7F7F7Fu;
-      uint32_t cur = 0;
-      for (int kt = 0; kt < KT; ++kt, ++it) {
-        if ((kt & 1) == 0) {
-          cur = w0;
-          w0 = w1;
-          const int nw = (kt >> 1) + 2;
-          if (valid && nw < nwords) w1 = ldg_nc_u32(srow + 4 * nw);
-        }
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-        if (!row_live) {
+      constexpr int kThreadsPerRow = (DECODE_WARPS * 32) / kP2HalfRows;  // 2 or 4
+      constexpr int kChunks = 8 / kThreadsPerRow;                         // 16-byte output chunks per thread
+      const int d = threadIdx.x - 256;
+      const int r = d / kThreadsPerRow;   // weight row in this CTA's half
+      const int part = d % kThreadsPerRow;
+      const int j0 = part * kChunks;      // first chunk (8 K values each)
+      const int blk_in_tile = j0 / 4;     // scale block (32 K) of this part within the 64-K stage
+      const uint32_t ready_leader = mapa_shared(smem_u32(ready), 0);
+      const bool row_live = r < half_rows;
+      int it = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        const PairTile c = pair_tile<EPI>(p, t, nmb);
+        bool valid;
+        const int64_t grow = pair_weight_row<EPI>(p, c, rank, r, valid);
+        valid = valid && row_live;
+        const uint8_t* srow = p.w_scales + (valid ? grow * p.lds : 0);
+        // one 32-bit scale word covers two 64-K stages; keep two words in flight
+        const int nwords = KT / 2;
+        uint32_t w0 = valid ? ldg_nc_u32(srow) : 0x7F7F7F7Fu;
+        uint32_t w1 = (valid && nwords > 1) ? ldg_nc_u32(srow + 4) : 0x7F7F7F7Fu;
+        uint32_t cur = 0;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          if ((kt & 1) == 0) {
+            cur = w0;
+            w0 = w1;
+            const int nw = (kt >> 1) + 2;
+            if (valid && nw < nwords) w1 = ldg_nc_u32(srow + 4 * nw);
+          }
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+          if (row_live) {
+            const uint32_t code = (cur >> (8 * ((kt & 1) * 2 + blk_in_tile))) & 0xFF;
+            const uint32_t psrc = smem_u32(smem + Cfg::kOffP + s * kP2PBytes) + r * 32 + j0 * 4;
+            const uint32_t bdst = smem_u32(smem + Cfg::kOffB + s * kP2BBytes) + r * 128;
+            const uint32_t sw = r & 7;
+            uint32_t w[kChunks];
+            if constexpr (kChunks == 4) {
+              const uint4 q4 = ld_shared_v4(psrc);
+              w[0] = q4.x;
+              w[1] = q4.y;
+              w[2] = q4.z;
+              w[3] = q4.w;
+            } else {
+              asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(psrc));
+            }
+            if (FP16) {
+              const float f = e8m0_to_f32(code);
+#pragma unroll
+              for (int i = 0; i < kChunks; ++i) st_shared_v4(bdst + (((j0 + i) ^ sw) << 4), decode8_f16(w[i], f));
+            } else {
+              const uint32_t b = e8m0_to_bf16x2(code);
+#pragma unroll
+              for (int i = 0; i < kChunks; ++i) st_shared_v4(bdst + (((j0 + i) ^ sw) << 4), decode8_bf16(w[i], b));
+            }
+            fence_proxy_async();
+          }
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(ready_leader + s * 8);
-          continue;
         }
-        const uint32_t code = (cur >> (8 * ((kt & 1) * 2 + blk_in_tile))) & 0xFF;
-        const uint32_t psrc = smem_u32(smem + Cfg::kOffP + s * kP2PBytes) + r * 32 + j0 * 4;
-        const uint32_t bdst = smem_u32(smem + Cfg::kOffB + s * kP2BBytes) + r * 128;
-        const uint32_t sw = r & 7;
-        uint32_t w[kChunks];
-        if constexpr (kChunks == 4) {
-          const uint4 q4 = ld_shared_v4(psrc);
-          w[0] = q4.x;
-          w[1] = q4.y;
-          w[2] = q4.z;
-          w[3] = q4.w;
-        } else {
-          asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(psrc));
-        }
-        if (FP16) {
-          const float f = e8m0_to_f32(code);
-#pragma unroll
-          for (int i = 0; i < kChunks; ++i) st_shared_v4(bdst + (((j0 + i) ^ sw) << 4), decode8_f16(w[i], f));
-        } else {
-          const uint32_t b = e8m0_to_bf16x2(code);
-#pragma unroll
-          for (int i = 0; i < kChunks; ++i) st_shared_v4(bdst + (((j0 + i) ^ sw) << 4), decode8_bf16(w[i], b));
-        }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(ready_leader + s * 8);
       }
-    }
     }
   }
 
