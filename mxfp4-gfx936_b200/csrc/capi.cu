@@ -143,6 +143,16 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
   return MXFP4_OK;
 }
 
+int run_gather(const void* x, int64_t k_elems, const int32_t* sorted_ids, const int32_t* post, int64_t routes,
+               int top_k, void* xr, int64_t cap, int sms, cudaStream_t stream) {
+  const int64_t row_vecs = k_elems * 2 / 16;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((cap + 7) / 8, int64_t(sms) * 16)));
+  gather_rows_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(x), row_vecs, sorted_ids, post,
+                                               static_cast<int>(routes), top_k, static_cast<uint4*>(xr), cap);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
 template <int AMODE, int BMODE, int EPI, bool FP16, int DW>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& p, int clusters,
                 cudaStream_t stream) {
@@ -473,6 +483,7 @@ size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_exp
   b += route_ws_bytes(routes, num_experts);
   const int cdt = c_dtype == MXFP4_DTYPE_F32 ? a_dtype : c_dtype;
   if (a_dtype != cdt || a_dtype == MXFP4_DTYPE_U8) b += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
+  b += align_up(static_cast<size_t>(cap) * k * 2, 256);  // activations in routed order
   return b;
 }
 
@@ -539,12 +550,18 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kP2BM, sorted_ids, block_expert, post, cap,
                          route_ws, s))
     return rc;
+  MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
+  if (a_eff != A) ws += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
+  void* a_routed = ws;
+  if (int rc = run_gather(a_eff, k, sorted_ids, post, routes, top_k, a_routed, cap, info.sms, s)) return rc;
 
-  CUtensorMap ta{}, tb;
+  CUtensorMap ta, tb;
+  const CUtensorMapDataType at = cdt == MXFP4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (int rc = make_map_2d(&ta, a_routed, at, 2, k, cap, k * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
   if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, static_cast<uint64_t>(num_experts) * n,
                            k / 2, kP2BK / 2, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
-  MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
   PairParams p{};
   p.N = static_cast<int>(n);
   p.K = static_cast<int>(k);
@@ -571,7 +588,7 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   p.c_stride_t = static_cast<int64_t>(top_k) * n;
   p.c_stride_j = n;
   p.vec_ok = aligned(C, 16) && (n * esz) % 16 == 0;
-  return routed_pair_gemm<A_GATHER, EPI_MOE>(cdt == MXFP4_DTYPE_F16, ta, tb, p, info.sms, s);
+  return routed_pair_gemm<A_TMA, EPI_MOE>(cdt == MXFP4_DTYPE_F16, ta, tb, p, info.sms, s);
 }
 
 // Same operation as mxfp4_fused_moe, with its scratch taken from the static
@@ -701,6 +718,7 @@ size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_exp
   b += route_ws_bytes(routes, num_experts);
   b += align_up(static_cast<size_t>(cap) * inter * 2, 256);     // h in routed order
   b += align_up(static_cast<size_t>(routes) * hidden * 2, 256); // weighted down rows
+  b += align_up(static_cast<size_t>(cap) * hidden * 2, 256);    // x in routed order
   return b;
 }
 
@@ -738,14 +756,20 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   void* hbuf = ws;
   ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
   void* ybuf = ws;
+  ws += align_up(static_cast<size_t>(routes) * hidden * 2, 256);
+  void* xbuf = ws;
 
   if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kP2BM, sorted_ids, block_expert, post, cap,
                          route_ws, s))
     return rc;
+  if (int rc = run_gather(x, hidden, sorted_ids, post, routes, top_k, xbuf, cap, info.sms, s)) return rc;
 
   // gate_up with fused SiLU(gate) * up -> h [cap, inter] in routed order
   {
-    CUtensorMap ta{}, tb;
+    CUtensorMap ta, tb;
+    if (int rc = make_map_2d(&ta, xbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hidden, cap, hidden * 2, kP2BK,
+                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
     if (int rc = make_map_2d(&tb, w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hidden / 2,
                              static_cast<uint64_t>(num_experts) * 2 * inter, hidden / 2, kP2BK / 2, kP2HalfRows,
                              CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -771,7 +795,7 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
     p.ldo = inter;
     p.out_dtype = MXFP4_DTYPE_BF16;
     p.vec_ok = 1;
-    if (int rc = routed_pair_gemm<A_GATHER, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
+    if (int rc = routed_pair_gemm<A_TMA, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
   }
   // down with route weights, scattered to y[route] = [routes, hidden]
   {

@@ -212,6 +212,30 @@ __global__ void __launch_bounds__(kRouteThreads) route_scatter_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Routed-order copy of the activations: xr[i] = x[sorted_ids[i] / top_k] for
+// every used position i < num_post_padded[0] that holds a route; pad rows are
+// left untouched (their GEMM rows are computed and discarded).  One warp per
+// row, 16-byte vectors; the grouped GEMM then loads A tiles with TMA.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restrict__ x, int64_t row_vecs,
+                                                          const int32_t* __restrict__ sorted_ids,
+                                                          const int32_t* __restrict__ num_post_padded,
+                                                          int num_routes, int top_k, uint4* __restrict__ xr,
+                                                          int64_t capacity) {
+  const int64_t posted = num_post_padded[0];
+  const int64_t used = posted < capacity ? posted : capacity;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); i < used; i += warps) {
+    const int route = sorted_ids[i];
+    if (route >= num_routes) continue;
+    const uint4* src = x + static_cast<int64_t>(route / top_k) * row_vecs;
+    uint4* dst = xr + i * row_vecs;
+    for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = src[v];
+  }
+}
+
+// ---------------------------------------------------------------------------
 // K5: out[t, :] = bf16( sum_j float(rows[t*top_k + j, :]) ), FP32 accumulation
 // in j order.  8 columns (16 bytes) per thread.
 // ---------------------------------------------------------------------------

@@ -35,7 +35,9 @@ template <int BMODE, int DECODE_WARPS>
 struct Pair2Cfg {
   static constexpr int kStages = 6;
   static constexpr int kDecodeWarps = BMODE == B_DECODE ? DECODE_WARPS : 0;
-  static constexpr int kThreads = 256 + 32 * kDecodeWarps;
+  // warps 0-3 control, 4-7 epilogue group 0, then the decoders, then epilogue group 1
+  static constexpr int kEpi1Warp = 8 + kDecodeWarps;
+  static constexpr int kThreads = 256 + 32 * kDecodeWarps + 128;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kP2ABytes;
   static constexpr int kOffP = kOffB + kStages * kP2BBytes;
@@ -233,7 +235,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);
+      mbar_init(&tempty[a], 16);  // 2 epilogue groups x 4 warps x 2 CTAs
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -368,9 +370,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
         }
     }
     __syncwarp();
-  } else if (warp >= 4 && warp < 8) {
+  } else if ((warp >= 4 && warp < 8) || (warp >= Cfg::kEpi1Warp && warp < Cfg::kEpi1Warp + 4)) {
     // ------------------------------------------------------------------ epilogue (both CTAs)
+    // two groups of four warps; warp w reads TMEM lane quarter w % 4 and group g
+    // takes the 32-column chunks cc with cc % 2 == g
     const int q = warp & 3;
+    const int grp = warp < 8 ? 0 : 1;
     const int r_local = q * 32 + lane;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
     const int esz = out_esize(p.out_dtype);
@@ -386,7 +391,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
         const bool row_ok = pos < p.M;
         uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(row_ok ? pos : 0) * p.ldo * esz;
 #pragma unroll 1
-        for (int cc = 0; cc < p.bn / 32; ++cc) {
+        for (int cc = grp; cc < p.bn / 32; cc += 2) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + cc * 32, r);
           tmem_ld_wait();
@@ -418,7 +423,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
                                     : 0;
         uint8_t* orow = static_cast<uint8_t*>(p.out) + roff * esz;
 #pragma unroll 1
-        for (int cc = 0; cc < p.bn / 32; ++cc) {
+        for (int cc = grp; cc < p.bn / 32; cc += 2) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + cc * 32, r);
           tmem_ld_wait();
@@ -436,7 +441,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
       } else {  // EPI_GLU: h = bf16(bf16(silu(bf16 g)) * bf16 u), written in routed order
         uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(pos) * p.ldo * 2;
 #pragma unroll 1
-        for (int cc = 0; cc < p.bn / 64; ++cc) {
+        for (int cc = grp; cc < p.bn / 64; cc += 2) {
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(tbase + cc * 32, g);
           tmem_ld_32x32b_x32(tbase + p.bn / 2 + cc * 32, u);
@@ -460,7 +465,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < Cfg::kEpi1Warp) {
     // ------------------------------------------------------------------ decoders (both CTAs)
     if constexpr (BMODE == B_DECODE) {
       constexpr int kThreadsPerRow = (DECODE_WARPS * 32) / kP2HalfRows;  // 2 or 4
