@@ -9,6 +9,7 @@
 #include "elementwise.cuh"
 #include "gemm.cuh"
 #include "gemm2.cuh"
+#include "gemm_small.cuh"
 #include "gemm_w4a4.cuh"
 
 using namespace mx;
@@ -126,6 +127,9 @@ int elem_size(int dtype) {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+constexpr int64_t kSmallMaxRows = 256;  // token counts served by the split-K few-token kernel
+constexpr int64_t kGemvRows = 2;        // token counts served by the CUDA-core GEMV (measured crossover)
+
 // --- GEMM launch ------------------------------------------------------------
 template <int AMODE, int BMODE, int EPI, bool FP16>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
@@ -177,6 +181,45 @@ int routed_pair_gemm(bool fp16, const CUtensorMap& ta, const CUtensorMap& tb, co
   const int clusters = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms / 2)));
   if (fp16) return launch_pair<AMODE, B_DECODE, EPI, true, 8>(ta, tb, p, clusters, stream);
   return launch_pair<AMODE, B_DECODE, EPI, false, 8>(ta, tb, p, clusters, stream);
+}
+
+// Few-token linear (M <= 256): swap-AB, K split over a cluster of `ks` CTAs.
+template <int BMODE, bool FP16>
+int launch_small(const CUtensorMap& tx, const CUtensorMap& tw, const SmallParams& p, cudaStream_t stream) {
+  auto kern = mxfp4_linear_small_kernel<BMODE, FP16>;
+  const int data = p.stages * p.stage_bytes;
+  const int part = kSmRows * p.mp * 4;
+  const int smem = ((data > part ? data : part) + 15) / 16 * 16 + 3 * kSmMaxStages * 8 + 64 + 1024;
+  MX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.ks, (p.N + kSmRows - 1) / kSmRows, 1);
+  cfg.blockDim = dim3(BMODE == B_DECODE ? 256 + 32 * kSmDecodeWarps : 256, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MX_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tw, p));
+  return MXFP4_OK;
+}
+
+template <int BMODE, bool FP16>
+int launch_gemv(const GemvParams& g, int sms, cudaStream_t stream) {
+  const int mr = g.M <= 1 ? 1 : 2;
+  const size_t smem = static_cast<size_t>(mr) * g.K * 2;
+  const int grid = static_cast<int>(std::min<int64_t>((g.N + 7) / 8, int64_t(sms) * 4));
+  auto go = [&](auto kern) -> int {
+    MX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    kern<<<grid, 256, smem, stream>>>(g);
+    MX_CUDA(cudaGetLastError());
+    return MXFP4_OK;
+  };
+  if (mr == 1) return go(mxfp4_gemv_kernel<1, BMODE, FP16>);
+  return go(mxfp4_gemv_kernel<2, BMODE, FP16>);
 }
 
 // Decode warps per CTA of the fused pair kernel (8 or 16, default 8); MXFP4_B200_DECODE_WARPS overrides.
@@ -380,6 +423,77 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   const CUtensorMapDataType xt = fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 
   CUtensorMap ta, tb;
+  if (m <= kGemvRows && static_cast<int64_t>(kGemvRows) * k * 2 <= 200 * 1024 && aligned(x, 16) &&
+      (ldx * 2) % 16 == 0 && aligned(w_packed, 16) && ldw % 16 == 0) {
+    GemvParams g{};
+    g.M = static_cast<int>(m);
+    g.N = static_cast<int>(n);
+    g.K = static_cast<int>(k);
+    g.x = x;
+    g.ldx = ldx;
+    g.out = out;
+    g.ldo = ldo;
+    g.out_dtype = x_dtype;
+    g.bias = bias;
+    if (mode == MXFP4_LINEAR_FUSED) {
+      g.w = static_cast<const uint8_t*>(w_packed);
+      g.ldw = ldw;
+      g.w_scales = static_cast<const uint8_t*>(w_scales);
+      g.lds = lds;
+      if (fp16) return launch_gemv<B_DECODE, true>(g, info.sms, s);
+      return launch_gemv<B_DECODE, false>(g, info.sms, s);
+    }
+    const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
+    MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
+    if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
+    g.w = static_cast<const uint8_t*>(workspace);
+    g.ldw = k * 2;
+    if (fp16) return launch_gemv<B_TMA, true>(g, info.sms, s);
+    return launch_gemv<B_TMA, false>(g, info.sms, s);
+  }
+  if (m <= kSmallMaxRows) {
+    SmallParams q{};
+    q.M = static_cast<int>(m);
+    q.N = static_cast<int>(n);
+    q.K = static_cast<int>(k);
+    q.mp = static_cast<int>((m + 31) / 32 * 32);
+    const int64_t row_blocks = (n + kSmRows - 1) / kSmRows;
+    const int64_t kt = k / kSmBK;
+    // the same stage layout (and so the same K split and summation order) in
+    // both modes: fused and safe results stay bit-identical
+    q.stage_bytes = q.mp * 128 + kSmWBytes + kSmPBytes;
+    q.stages = static_cast<int>(std::max(2, std::min(kSmMaxStages, (200 * 1024) / q.stage_bytes)));
+    // K splits: the largest cluster (<= 8) whose CTAs fit one CTA per SM
+    int ks = 1;
+    for (int c = 8; c >= 1; --c)
+      if (row_blocks * c <= info.sms && c <= kt) { ks = c; break; }
+    q.ks = ks;
+    q.w_scales = static_cast<const uint8_t*>(w_scales);
+    q.lds = lds;
+    q.out = out;
+    q.ldo = ldo;
+    q.out_dtype = x_dtype;
+    q.bias = bias;
+    if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kSmBK, q.mp, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+    if (mode == MXFP4_LINEAR_FUSED) {
+      if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kSmBK / 2, kSmRows,
+                               CU_TENSOR_MAP_SWIZZLE_NONE))
+        return rc;
+      if (fp16) return launch_small<B_DECODE, true>(ta, tb, q, s);
+      return launch_small<B_DECODE, false>(ta, tb, q, s);
+    }
+    const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
+    MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
+    if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
+    if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kSmBK, kSmRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (fp16) return launch_small<B_TMA, true>(ta, tb, q, s);
+    return launch_small<B_TMA, false>(ta, tb, q, s);
+  }
   if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
 
   PairParams p{};
