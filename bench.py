@@ -17,7 +17,11 @@ At N=1 the other BASELINE configurations are measured as ``extra`` entries
 (o_proj, the decode sweep, the safe mode, the MoE layer of config 2).  With
 N>1 ranks (torchrun, NCCL) the headline is the column-sharded linear: each
 rank owns N/G output columns and an NCCL all-gather assembles the output
-(strong scaling, total work fixed).
+(strong scaling, total work fixed); its ``roofline`` is the shard GEMM's and
+``step_roofline`` is the slower of that GEMM at the bf16 peak and the
+all-gather bytes at the measured NVLink rate.  The expert-parallel MoE layer
+(config 2, T/G tokens and E/G experts per rank, NCCL all-to-all dispatch and
+combine) is reported as an ``extra`` entry.
 
 ``--impl reference`` times the reference's safe path restated with PyTorch CPU
 ops (oracle/ref_cpu.py) on this machine's host cores for the same workload; the
@@ -160,25 +164,38 @@ def make_linear_inputs(m, n, k, seed, device):
 
 
 def graphs_for(fn, sets, stream):
-    """One CUDA graph per input set, each holding one step."""
-    gs = []
+    """CUDA graphs for the timed loop: one graph holding one step per input set
+    (the whole rotation, replayed as a unit) plus one single-step graph per
+    set for a step count that is not a multiple of the rotation."""
     for args in sets:
         fn(*args)  # warm the allocator and one-time attributes outside capture
     torch.cuda.synchronize()
+    singles = []
     for args in sets:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             fn(*args)
-        gs.append(g)
+        singles.append(g)
+    rotation = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(rotation, stream=stream):
+        for args in sets:
+            fn(*args)
     torch.cuda.synchronize()
-    return gs
+    return {"rotation": rotation, "singles": singles}
+
+
+def _replay_steps(gs, steps):
+    r = len(gs["singles"])
+    for _ in range(steps // r):
+        gs["rotation"].replay()
+    for i in range(steps % r):
+        gs["singles"][i].replay()
 
 
 def time_graphs(gs, steps, warmup, barrier=None, sampler=None):
-    """Replay rotating graphs; returns ms per step measured with CUDA events."""
+    """Replay the rotation; returns ms per step measured with CUDA events."""
     stream = torch.cuda.current_stream()
-    for i in range(warmup):
-        gs[i % len(gs)].replay()
+    _replay_steps(gs, warmup)
     torch.cuda.synchronize()
     if barrier:
         barrier()
@@ -187,8 +204,7 @@ def time_graphs(gs, steps, warmup, barrier=None, sampler=None):
     ctx = sampler if sampler is not None else _Null()
     with ctx:
         start.record(stream)
-        for i in range(steps):
-            gs[i % len(gs)].replay()
+        _replay_steps(gs, steps)
         end.record(stream)
         end.synchronize()
     torch.cuda.synchronize()
@@ -384,7 +400,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE config-1 distributions, seeded)",
         "config": {"workload": "config1_qkv_prefill", "M": m, "N": n, "K": k, "backend": "fused",
-                   "l2": "4 rotating input sets of 64 MB (working set > 126 MB L2)", "timing": "CUDA-graph replays, CUDA events",
+                   "l2": "4 rotating input sets of 64 MB (working set > 126 MB L2)", "timing": "CUDA graph of the 4-set rotation replayed, CUDA events",
                    "parallelism": "single GPU"},
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": tflops / pk["bf16_tflops"], "traffic": profile_traffic("linear_fused_qkv"),
@@ -449,40 +465,147 @@ def run_one(args, soft, device):
     return 0
 
 
+NVLINK_GBS = 770.0   # measured peer copy per direction per GPU on this pool (nominal 900)
+
+
+def _max_over_ranks(v, device):
+    import torch.distributed as dist
+    t = torch.tensor([v], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def bench_ep_moe(soft, ep_mod, world, rank, device, steps, warmup, barrier):
+    """Expert-parallel config-2 layer: T tokens in total, T/G per rank, E/G experts per rank."""
+    t_local = MOE["t"] // world
+    x, w13, s13, w2, s2, tw, tid = make_moe_inputs(device, seed=7, **MOE)
+    sl = slice(rank * t_local, (rank + 1) * t_local)
+    layer = ep_mod.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world)
+    xs, tws, tids = x[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous()
+    del w13, s13, w2, s2, x, tw, tid
+    for _ in range(warmup):
+        layer(xs, tws, tids)
+    torch.cuda.synchronize()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        layer(xs, tws, tids)
+    end.record()
+    end.synchronize()
+    barrier()
+    ms = _max_over_ranks(start.elapsed_time(end) / steps, device)
+    routes_local = t_local * MOE["k"]
+    # bytes a rank must receive over NVLink per step: dispatched rows from the
+    # other ranks plus their combined rows coming back (uniform routing)
+    nv_bytes = 2 * routes_local * (world - 1) / world * MOE["h"] * 2
+    return ms, nv_bytes, moe_flops()
+
+
 def run_sharded(args, soft, world, rank, device, pk, pk_kind):
+    """N>1: the column-sharded dense linear (headline) and the expert-parallel
+    MoE layer (extra), one process per GPU over NCCL."""
     import datetime
 
     import torch.distributed as dist
 
     dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     cp = _load("mxfp4_column_parallel", PKG / "column_parallel.py")
+    ep_mod = _load("mxfp4_expert_parallel", PKG / "expert_parallel.py")
     m, n, k = QKV
     set_backend("fused")
-    sets = []
+    barrier = lambda: dist.barrier(device_ids=[device.index])  # noqa: E731
+    sets, shard_sets = [], []
     for i in range(4):
         x, w, s = make_linear_inputs(m, n, k, i, device)  # same full weight on every rank
-        sets.append((x, cp.ColumnParallelLinear.from_full(w, s, rank, world)))
-    barrier = lambda: dist.barrier(device_ids=[device.index])  # noqa: E731
+        layer = cp.ColumnParallelLinear.from_full(w, s, rank, world)
+        sets.append((x, layer))
+        shard_sets.append((x, layer.w, layer.s))
+        del w, s
+    # the shard GEMM alone (the dominant kernel), then GEMM + all-gather
+    gs_local = graphs_for(lambda x, w, s: soft.linear_mxfp4_soft(x, w, s), shard_sets, torch.cuda.Stream())
+    ms_gemm = _max_over_ranks(time_graphs(gs_local, args.steps, args.warmup, barrier=barrier), device)
+    del gs_local
     gs = graphs_for(lambda x, layer: layer(x), sets, torch.cuda.Stream())
-    ms_local = time_graphs(gs, args.steps, args.warmup, barrier=barrier)
-    t = torch.tensor([ms_local], device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t.item()
+    sampler = ClockSampler(device.index)
+    ms = _max_over_ranks(time_graphs(gs, args.steps, args.warmup, barrier=barrier, sampler=sampler), device)
+    del gs
     flops = 2.0 * m * n * k
     tflops = flops / (ms * 1e-3) / 1e12
+    shard_flops = flops / world
+    gemm_tflops = shard_flops / (ms_gemm * 1e-3) / 1e12
+    # step roofline: the slower of the shard GEMM at the bf16 peak and the
+    # all-gather bytes each GPU must receive at the measured NVLink rate
+    ag_bytes = 2.0 * m * n * (world - 1) / world
+    t_tensor = shard_flops / (pk["bf16_tflops"] * 1e12)
+    t_nvlink = ag_bytes / (NVLINK_GBS * 1e9)
+    t_roof = max(t_tensor, t_nvlink)
+
+    # end to end: pinned host activations in, gathered output back to the host
+    x_host = sets[0][0].cpu().pin_memory()
+    y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+    layer0 = sets[0][1]
+
+    def e2e_step():
+        xd = x_host.to(device, non_blocking=True)
+        y_host.copy_(layer0(xd), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e_steps = max(10, args.steps // 4)
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    st.record()
+    for _ in range(e_steps):
+        e2e_step()
+    en.record()
+    en.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3 / e_steps
+    e2e_ms = _max_over_ranks(max(st.elapsed_time(en) / e_steps, wall), device)
+    barrier()
+    del sets, shard_sets
+
+    # expert-parallel MoE layer (config 2, tokens data-parallel across ranks)
+    ep_steps = max(5, min(20, args.steps // 10))
+    ms_ep, ep_nv_bytes, fm = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup, barrier)
+    t_ep_roof = max(fm / world / (pk["bf16_tflops"] * 1e12), ep_nv_bytes / (NVLINK_GBS * 1e9))
+    status = soft.device_status()
+    status = int(_max_over_ranks(float(status), device))
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE config-1 distributions, seeded)",
             "config": {"workload": "config1_qkv_prefill", "M": m, "N": n, "K": k, "backend": "fused",
-                       "parallelism": f"tp{world} column-sharded + NCCL all-gather",
-                       "l2": "4 rotating input sets"},
-            "roofline": None, "gpu_launches": args.steps,
+                       "parallelism": f"tp{world}: column-sharded W (N/{world} rows per GPU) + NCCL all-gather",
+                       "l2": "4 rotating input sets of 64 MB (working set > 126 MB L2)",
+                       "timing": "CUDA graph of the 4-set rotation replayed, CUDA events, max over ranks"},
+            "roofline": {"bound": "tensor", "achieved": gemm_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": gemm_tflops / pk["bf16_tflops"], "traffic": None,
+                         "kernel": f"shard GEMM {m}x{n // world}x{k}",
+                         "peak_source": f"{pk_kind} bf16 burst"},
+            "step_roofline": {"bound": "nvlink" if t_nvlink > t_tensor else "tensor",
+                              "target_ms": t_roof * 1e3, "frac": t_roof * 1e3 / ms,
+                              "allgather_bytes_in_per_gpu": ag_bytes, "nvlink_gbs": NVLINK_GBS,
+                              "shard_gemm_ms": ms_gemm},
+            "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2},
+            "gpu_launches": args.steps,
+            "clocks": sampler.result(),
+            "extra": {"config2_moe_layer_ep": {
+                "ms": ms_ep, "tokens_per_s": MOE["t"] / (ms_ep * 1e-3), "tflops": fm / ms_ep / 1e9,
+                "experts_per_gpu": MOE["e"] // world, "tokens_per_gpu": MOE["t"] // world,
+                "roofline_target_ms": t_ep_roof * 1e3, "roofline_frac": t_ep_roof * 1e3 / ms_ep,
+                "nvlink_bytes_in_per_gpu": ep_nv_bytes,
+                "timing": "CUDA events around eager calls (host syncs on the per-destination counts), max over ranks"}},
         }
+        if status:
+            line["device_status"] = status
         print(json.dumps(line), flush=True)
-    del gs
-    dist.barrier(device_ids=[device.index])
+    barrier()
     dist.destroy_process_group()
     return 0
 

@@ -1,0 +1,132 @@
+"""Expert-parallel MXFP4 MoE layer over torch.distributed (NCCL on GPUs).
+
+Each of the G ranks owns E/G consecutive experts (global ids
+``[rank*E/G, (rank+1)*E/G)``) and its own tokens.  One layer call:
+
+1. routes ``r = t*top_k + j`` are grouped by destination rank
+   ``topk_ids // (E/G)`` with the device routing kernel (K4, ranks as
+   "experts", block size 1: stable, no padding);
+2. per-destination counts are exchanged, then one all-to-all each carries the
+   activation row ``x[r // top_k]``, the local expert id and the route weight
+   (dispatch);
+3. the owner runs the MoE layer (K3 gate_up with fused SiLU*up, K3 down with
+   the route weight) on its received routes, one route per row;
+4. the weighted rows travel back with the reverse all-to-all (combine) and the
+   top-k rows of every token are summed in FP32 in slot order and rounded to
+   BF16 -- the same order as the single-GPU combine kernel, so the result is
+   bit-identical to the single-GPU layer.
+
+This is the expert-parallel form of the reference's MoE composition
+(integration/vllm/vllm_mxfp4_gfx936.py:233-265), whose only EP-aware code is
+the rule that routes to non-local experts produce nothing locally
+(src/aiter/ops/triton/moe_op_mxfp4_soft.py:113-115, 478).
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+_HERE = Path(__file__).resolve().parent
+
+
+def _soft():
+    name = "moe_op_mxfp4_soft"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(name, _HERE / "moe_op_mxfp4_soft.py")
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules[name]
+
+
+def expert_range(num_experts: int, rank: int, world: int) -> tuple[int, int]:
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not divide over {world} ranks")
+    per = num_experts // world
+    return rank * per, (rank + 1) * per
+
+
+def sum_topk_rows(rows: torch.Tensor, top_k: int) -> torch.Tensor:
+    """out[t] = bf16(sum_j float(rows[t*top_k + j])), FP32 accumulation in j order."""
+    t = rows.shape[0] // top_k
+    r = rows.view(t, top_k, -1)
+    acc = r[:, 0].float()
+    for j in range(1, top_k):
+        acc = acc + r[:, j].float()
+    return acc.to(torch.bfloat16)
+
+
+class ExpertParallelMoE:
+    """One rank's share of an expert-parallel MXFP4 MoE layer.
+
+    ``layer_fn(x, w13, s13, w2, s2, topk_weights, topk_ids)`` computes the
+    local layer (default: the native ``moe_layer_mxfp4``); ``route_fn(ids,
+    num_groups)`` returns the stable destination order of the routes (default:
+    the device routing kernel).  Both are injectable so the exchange logic can
+    be tested on CPU ranks.
+    """
+
+    def __init__(self, w13_local, s13_local, w2_local, s2_local, num_experts: int, rank: int, world: int,
+                 group=None, layer_fn=None, route_fn=None):
+        self.w13, self.s13, self.w2, self.s2 = w13_local, s13_local, w2_local, s2_local
+        self.num_experts, self.rank, self.world, self.group = num_experts, rank, world, group
+        self.lo, self.hi = expert_range(num_experts, rank, world)
+        self.per = self.hi - self.lo
+        if w13_local.shape[0] != self.per or w2_local.shape[0] != self.per:
+            raise ValueError("local weights must hold num_experts / world experts")
+        self.layer_fn = layer_fn if layer_fn is not None else _soft().moe_layer_mxfp4
+        self.route_fn = route_fn if route_fn is not None else self._device_route
+
+    @classmethod
+    def from_full(cls, w13, s13, w2, s2, rank: int, world: int, group=None, layer_fn=None, route_fn=None):
+        lo, hi = expert_range(w13.shape[0], rank, world)
+        return cls(w13[lo:hi].contiguous(), s13[lo:hi].contiguous(), w2[lo:hi].contiguous(),
+                   s2[lo:hi].contiguous(), w13.shape[0], rank, world, group, layer_fn, route_fn)
+
+    @staticmethod
+    def _device_route(dest: torch.Tensor, world: int) -> torch.Tensor:
+        sorted_ids, _, post = _soft().moe_route(dest.view(-1, 1), world, block_m=1)
+        return sorted_ids[: dest.numel()].long()
+
+    def __call__(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+        t, hidden = x.shape
+        top_k = topk_ids.shape[1]
+        ids = topk_ids.reshape(-1).long()
+        dest = (ids // self.per).to(torch.int32)
+        order = self.route_fn(dest, self.world)                      # routes grouped by destination
+        counts = torch.bincount(dest.long(), minlength=self.world)   # routes per destination
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        send_sizes = counts.tolist()
+        recv_sizes = recv_counts.tolist()
+        n_recv = int(sum(recv_sizes))
+
+        # dispatch: activation rows, local expert ids, route weights
+        x_send = x.index_select(0, torch.div(order, top_k, rounding_mode="floor"))
+        e_send = (ids.index_select(0, order) - dest.long().index_select(0, order) * self.per).to(torch.int32)
+        w_send = topk_weights.reshape(-1).float().index_select(0, order)
+        x_recv = torch.empty((n_recv, hidden), dtype=x.dtype, device=x.device)
+        e_recv = torch.empty((n_recv,), dtype=torch.int32, device=x.device)
+        w_recv = torch.empty((n_recv,), dtype=torch.float32, device=x.device)
+        dist.all_to_all_single(x_recv, x_send, recv_sizes, send_sizes, group=self.group)
+        dist.all_to_all_single(e_recv, e_send, recv_sizes, send_sizes, group=self.group)
+        dist.all_to_all_single(w_recv, w_send, recv_sizes, send_sizes, group=self.group)
+
+        # local experts, one route per row (top_k = 1): y = bf16(bf16(h . W2^T) * w)
+        if n_recv:
+            y_recv = self.layer_fn(x_recv, self.w13, self.s13, self.w2, self.s2, w_recv.view(-1, 1),
+                                   e_recv.view(-1, 1))
+        else:                                                         # no route chose this rank's experts
+            y_recv = torch.empty((0, hidden), dtype=torch.bfloat16, device=x.device)
+
+        # combine: weighted rows back to their origin, unpermute, sum over top-k
+        y_send = torch.empty((ids.numel(), hidden), dtype=y_recv.dtype, device=x.device)
+        dist.all_to_all_single(y_send, y_recv.contiguous(), send_sizes, recv_sizes, group=self.group)
+        y_routes = torch.empty_like(y_send)
+        y_routes.index_copy_(0, order, y_send)
+        return sum_topk_rows(y_routes, top_k)

@@ -57,3 +57,64 @@ def test_shard_rows_rejects_uneven_split():
     assert cp.shard_rows(5120, 7, 8) == (4480, 5120)
     with pytest.raises(ValueError):
         cp.shard_rows(100, 0, 3)
+
+
+# ---------------------------------------------------------------------------
+# expert parallelism: dispatch / combine exchange on CPU ranks
+# ---------------------------------------------------------------------------
+def _ep_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ep = load_by_path("mxfp4_expert_parallel", PKG / "expert_parallel.py")
+        ref = load_by_path("mxfp4_ref_cpu", ROOT / "oracle" / "ref_cpu.py")
+        O = load_by_path("mxfp4_oracle", ROOT / "oracle" / "mxfp4_oracle.py")
+        g = torch.Generator().manual_seed(3)
+        t_local, h, e, k, inter = 12, 256, 8, 2, 128
+        x_all = torch.randn(world * t_local, h, generator=g).to(torch.bfloat16)
+        w13 = torch.randint(0, 256, (e, 2 * inter, h // 2), generator=g, dtype=torch.uint8)
+        s13 = torch.randint(118, 131, (e, 2 * inter, h // 32), generator=g, dtype=torch.uint8)
+        w2 = torch.randint(0, 256, (e, h, inter // 2), generator=g, dtype=torch.uint8)
+        s2 = torch.randint(114, 127, (e, h, inter // 32), generator=g, dtype=torch.uint8)
+        logits = torch.randn(world * t_local, e, generator=g)
+        tw_all, tid_all = torch.topk(torch.softmax(logits, -1), k, dim=-1)
+        sl = slice(rank * t_local, (rank + 1) * t_local)
+
+        def route_fn(dest, world_):
+            return torch.argsort(dest.long(), stable=True)
+
+        layer = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, layer_fn=ref.moe_layer,
+                                               route_fn=route_fn)
+        y = layer(x_all[sl], tw_all[sl], tid_all[sl])
+        full = ref.moe_layer(x_all, w13, s13, w2, s2, tw_all, tid_all)[sl]
+        ok = O.check_close(y.float().numpy(), full.float().numpy())[0]
+        # one rank's tokens may route only to the other rank's experts and vice versa
+        q.put((rank, bool(ok), tuple(y.shape)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_matches_single_layer_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    results = {r: (ok, shp) for r, ok, shp in (q.get(timeout=5) for _ in procs)}
+    assert results == {0: (True, (12, 256)), 1: (True, (12, 256))}
+    assert all(p.exitcode == 0 for p in procs)
+
+
+def test_expert_range_and_topk_sum():
+    ep = load_by_path("mxfp4_expert_parallel", PKG / "expert_parallel.py")
+    assert ep.expert_range(128, 3, 8) == (48, 64)
+    with pytest.raises(ValueError):
+        ep.expert_range(10, 0, 4)
+    rows = torch.randn(6, 16).to(torch.bfloat16)
+    s = ep.sum_topk_rows(rows, 3)
+    want = (rows.view(2, 3, 16).float()[:, 0] + rows.view(2, 3, 16).float()[:, 1]
+            + rows.view(2, 3, 16).float()[:, 2]).to(torch.bfloat16)
+    assert torch.equal(s.view(torch.int16), want.view(torch.int16))

@@ -1,0 +1,78 @@
+"""Multi-GPU paths on real GPUs (NCCL over NVLink): the column-sharded linear
+and the expert-parallel MoE layer must reproduce the single-GPU results bit
+for bit.  Skipped on machines with fewer than two GPUs."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from _paths import PKG, load_by_path
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        soft = load_by_path("moe_op_mxfp4_soft", PKG / "moe_op_mxfp4_soft.py")
+        cp = load_by_path("mxfp4_column_parallel", PKG / "column_parallel.py")
+        ep = load_by_path("mxfp4_expert_parallel", PKG / "expert_parallel.py")
+        os.environ["MXFP4_GFX936_BACKEND"] = "fused"
+        g = torch.Generator(device=dev).manual_seed(11)
+        # column-sharded dense linear
+        m, n, k = 300, 2048, 1024
+        x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.randint(0, 256, (n, k // 2), generator=g, device=dev, dtype=torch.uint8)
+        s = torch.randint(118, 131, (n, k // 32), generator=g, device=dev, dtype=torch.uint8)
+        y_tp = cp.ColumnParallelLinear.from_full(w, s, rank, world)(x)
+        y_one = soft.linear_mxfp4_soft(x, w, s)
+        # the shard GEMMs see different N, so tiles differ; each output is one
+        # FP32 reduction of the same products in K order
+        lin_ok = bool(torch.equal(y_tp.view(torch.int16), y_one.view(torch.int16)))
+        # expert-parallel MoE: every rank owns its tokens and E/world experts
+        t_local, h, e, top_k, inter = 512, 1024, 32, 4, 256
+        x_all = torch.randn(world * t_local, h, generator=g, device=dev).to(torch.bfloat16)
+        w13 = torch.randint(0, 256, (e, 2 * inter, h // 2), generator=g, device=dev, dtype=torch.uint8)
+        s13 = torch.randint(118, 131, (e, 2 * inter, h // 32), generator=g, device=dev, dtype=torch.uint8)
+        w2 = torch.randint(0, 256, (e, h, inter // 2), generator=g, device=dev, dtype=torch.uint8)
+        s2 = torch.randint(118, 131, (e, h, inter // 32), generator=g, device=dev, dtype=torch.uint8)
+        tw, tid = torch.topk(torch.softmax(torch.randn(world * t_local, e, generator=g, device=dev), -1), top_k, -1)
+        sl = slice(rank * t_local, (rank + 1) * t_local)
+        layer = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world)
+        y_ep = layer(x_all[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous())
+        y_full = soft.moe_layer_mxfp4(x_all, w13, s13, w2, s2, tw, tid)[sl]
+        ep_ok = bool(torch.equal(y_ep.view(torch.int16), y_full.view(torch.int16)))
+        torch.cuda.synchronize()
+        q.put((rank, lin_ok, ep_ok, soft.device_status()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_column_parallel_and_expert_parallel_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    res = sorted(q.get(timeout=5) for _ in procs)
+    assert all(p.exitcode == 0 for p in procs)
+    assert res == [(0, True, True, 0), (1, True, True, 0)], res
