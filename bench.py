@@ -369,7 +369,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the non-headline configurations")
-    ap.add_argument("--workload", default=None, choices=["oproj", "safe", "decode", "moe", "w4a4"],
+    ap.add_argument("--workload", default=None, choices=["qkv", "oproj", "safe", "decode", "moe", "w4a4"],
                     help="run only this configuration (for profiling); prints its timing as JSON")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -451,7 +451,9 @@ def main():
 def run_one(args, soft, device):
     """One configuration on its own (profiling aid; not the driver's line)."""
     w = args.workload
-    if w == "oproj":
+    if w == "qkv":
+        ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "fused", device)
+    elif w == "oproj":
         ms = bench_linear(soft, OPROJ, args.steps, args.warmup, 4, "fused", device, seed0=10)
     elif w == "safe":
         ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "safe", device, seed0=20)

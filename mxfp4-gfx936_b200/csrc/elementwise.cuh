@@ -118,82 +118,99 @@ __global__ void __launch_bounds__(kRouteThreads) route_count_kernel(
   if (r < num_routes) rank_out[r] = e >= 0 ? warp_cnt[warp * num_experts + e] + rank_in_warp : -1;
 }
 
-// One CTA of 1024 threads.  hist[c][e] -> per-chunk bases (in place, exclusive
-// prefix over chunks per expert); blk_off[e] = first block of expert e
-// (exclusive scan of the padded block counts); writes the per-block expert ids,
-// the pad entries and the used length.  The histogram is staged through
-// shared memory in tiles of rows so every global access is coalesced.
-__global__ void __launch_bounds__(1024) route_offsets_kernel(
-    int32_t* __restrict__ hist, int num_chunks, int num_experts, int block_m, int64_t num_routes,
-    int32_t* __restrict__ blk_off, int32_t* __restrict__ sorted_ids,
-    int32_t* __restrict__ block_expert, int32_t* __restrict__ num_post_padded,
-    int64_t capacity_blocks) {
-  constexpr int kTileElems = 8192;  // 32 KB of counts per tile
-  __shared__ int32_t tile[kTileElems];
-  __shared__ int32_t total_s[kMaxExperts];
-  __shared__ int32_t scan_s[kMaxExperts];
-  __shared__ int32_t warp_sums[32];
-  const int rows_per_tile = kTileElems / num_experts > 0 ? kTileElems / num_experts : 1;
-  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) total_s[e] = 0;
-  __syncthreads();
-  for (int c0 = 0; c0 < num_chunks; c0 += rows_per_tile) {
-    const int rows = min(rows_per_tile, num_chunks - c0);
-    const int n = rows * num_experts;
-    int32_t* g = hist + static_cast<int64_t>(c0) * num_experts;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) tile[i] = g[i];
-    __syncthreads();
-    for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
-      int run = total_s[e];
-      for (int c = 0; c < rows; ++c) {
-        const int v = tile[c * num_experts + e];
-        tile[c * num_experts + e] = run;
-        run += v;
-      }
-      total_s[e] = run;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) g[i] = tile[i];
-    __syncthreads();
-  }
-  // exclusive scan of padded block counts over experts (E <= 1024: one per thread)
-  const int e = threadIdx.x;
-  const int nb = e < num_experts ? (total_s[e] + block_m - 1) / block_m : 0;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  int incl = nb;
+// One CTA of 1024 threads (32 warps).  hist[c][e] -> per-chunk bases (in
+// place: exclusive prefix over chunks per expert); blk_off[e] = first block of
+// expert e (exclusive scan of the padded block counts); writes the per-block
+// expert ids, the pad entries and the used length.  The histogram moves
+// through shared memory in tiles of whole chunk rows (coalesced loads and
+// stores, row stride E+1 so the column walks below are conflict-free); in a
+// tile, warp w scans the chunk column of experts w, w+32, ... with its lanes
+// on contiguous row ranges, carrying each expert's running total across tiles.
+__device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
+  int incl = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
     if (lane >= o) incl += y;
   }
-  if (lane == 31) warp_sums[wid] = incl;
+  total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+  return incl - v;
+}
+
+constexpr int kOffsetsTileInts = 9216;  // 36 KB of counts per tile
+
+__global__ void __launch_bounds__(1024) route_offsets_kernel(
+    int32_t* __restrict__ hist, int num_chunks, int num_experts, int block_m, int64_t num_routes,
+    int32_t* __restrict__ blk_off, int32_t* __restrict__ sorted_ids,
+    int32_t* __restrict__ block_expert, int32_t* __restrict__ num_post_padded,
+    int64_t capacity_blocks) {
+  __shared__ int32_t tile[kOffsetsTileInts];
+  __shared__ int32_t total_s[kMaxExperts];
+  __shared__ int32_t scan_s[kMaxExperts];
+  __shared__ int32_t warp_sums[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int ld = num_experts + 1;
+  const int rows_per_tile = kOffsetsTileInts / ld > 0 ? kOffsetsTileInts / ld : 1;
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) total_s[e] = 0;
+  for (int c0 = 0; c0 < num_chunks; c0 += rows_per_tile) {
+    const int rows = min(rows_per_tile, num_chunks - c0);
+    const int n = rows * num_experts;
+    int32_t* g = hist + static_cast<int64_t>(c0) * num_experts;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) tile[(i / num_experts) * ld + i % num_experts] = g[i];
+    __syncthreads();
+    const int per = (rows + 31) / 32;
+    const int r_beg = min(lane * per, rows), r_end = min(r_beg + per, rows);
+    for (int e = wid; e < num_experts; e += 32) {
+      int sum = 0;
+      for (int r = r_beg; r < r_end; ++r) sum += tile[r * ld + e];
+      int total;
+      int run = warp_excl_scan(sum, lane, total) + total_s[e];
+      for (int r = r_beg; r < r_end; ++r) {
+        const int v = tile[r * ld + e];
+        tile[r * ld + e] = run;
+        run += v;
+      }
+      __syncwarp();
+      if (lane == 0) total_s[e] += total;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) g[i] = tile[(i / num_experts) * ld + i % num_experts];
+    __syncthreads();
+  }
+  __syncthreads();
+  // exclusive scan of padded block counts over experts (E <= 1024: one per thread)
+  const int e = threadIdx.x;
+  const int nb = e < num_experts ? (total_s[e] + block_m - 1) / block_m : 0;
+  int blocks_total;
+  const int excl_in_warp = warp_excl_scan(nb, lane, blocks_total);
+  if (lane == 0) warp_sums[wid] = blocks_total;
   __syncthreads();
   if (wid == 0) {
-    int w = warp_sums[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xFFFFFFFFu, w, o);
-      if (lane >= o) w += y;
-    }
-    warp_sums[lane] = w;  // inclusive over warps
+    int t;
+    const int ex = warp_excl_scan(warp_sums[lane], lane, t);
+    warp_sums[lane] = ex;  // exclusive over warps
+    if (lane == 0) num_post_padded[0] = t * block_m;
   }
   __syncthreads();
-  const int excl = incl - nb + (wid > 0 ? warp_sums[wid - 1] : 0);
-  if (e < num_experts) scan_s[e] = excl;
-  const int total_blocks = warp_sums[31];
-  if (threadIdx.x == 0) num_post_padded[0] = total_blocks * block_m;
-  for (int64_t b = total_blocks + threadIdx.x; b < capacity_blocks; b += blockDim.x) block_expert[b] = -1;
-  __syncthreads();
-  const int32_t pad = static_cast<int32_t>(num_routes);
+  const int excl = excl_in_warp + warp_sums[wid];
   if (e < num_experts) {
+    scan_s[e] = excl;
     blk_off[e] = excl;
-    for (int b = 0; b < nb; ++b) block_expert[excl + b] = e;
   }
-  // pad entries of every expert's last block: spread over all threads
-  for (int x = 0; x < num_experts; ++x) {
-    const int beg_in = total_s[x];
-    const int end_in = ((beg_in + block_m - 1) / block_m) * block_m;
-    const int64_t base = static_cast<int64_t>(scan_s[x]) * block_m;
-    for (int i = beg_in + threadIdx.x; i < end_in; i += blockDim.x) sorted_ids[base + i] = pad;
+  __syncthreads();
+  const int used_blocks = num_experts > 0 ? scan_s[num_experts - 1] +
+                                                (total_s[num_experts - 1] + block_m - 1) / block_m
+                                          : 0;
+  for (int64_t b = used_blocks + threadIdx.x; b < capacity_blocks; b += blockDim.x) block_expert[b] = -1;
+  // per-block expert ids and the pad entries of every expert's last block: warp per expert
+  const int32_t pad = static_cast<int32_t>(num_routes);
+  for (int x = wid; x < num_experts; x += 32) {
+    const int cnt = total_s[x];
+    const int nbx = (cnt + block_m - 1) / block_m;
+    const int first = scan_s[x];
+    for (int b = lane; b < nbx; b += 32) block_expert[first + b] = x;
+    const int64_t base = static_cast<int64_t>(first) * block_m;
+    for (int i = cnt + lane; i < nbx * block_m; i += 32) sorted_ids[base + i] = pad;
   }
 }
 
