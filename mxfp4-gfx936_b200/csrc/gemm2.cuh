@@ -160,11 +160,21 @@ struct PairTile {
   int m_blk, n_blk, expert;
 };
 
+// Tile order.  Dense: row blocks fastest, so the clusters in flight share each
+// weight tile through L2 and the activations (at most a few tens of MB) stay
+// in L2 anyway.  Routed: column blocks fastest, so the (large) routed
+// activation block is read from HBM once and reused from L2 by its column
+// tiles, and the weights of an expert's consecutive route blocks are shared.
 template <int EPI>
 __device__ __forceinline__ PairTile pair_tile(const PairParams& p, int t, int nmb) {
   PairTile c;
-  c.m_blk = t % nmb;
-  c.n_blk = t / nmb;
+  if (EPI == EPI_DENSE) {
+    c.m_blk = t % nmb;
+    c.n_blk = t / nmb;
+  } else {
+    c.m_blk = t / p.num_n_blocks;
+    c.n_blk = t % p.num_n_blocks;
+  }
   c.expert = EPI == EPI_DENSE ? 0 : p.block_expert[c.m_blk];
   return c;
 }
