@@ -131,22 +131,6 @@ constexpr int64_t kSmallMaxRows = 256;  // token counts served by the split-K fe
 constexpr int64_t kGemvRows = 2;        // token counts served by the CUDA-core GEMV (measured crossover)
 
 // --- GEMM launch ------------------------------------------------------------
-template <int AMODE, int BMODE, int EPI, bool FP16>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
-                cudaStream_t stream) {
-  using Cfg = GemmCfg<BMODE>;
-  auto kern = mxfp4_gemm_kernel<AMODE, BMODE, EPI, FP16>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-  });
-  MX_CUDA(attr_err);
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
-  MX_CUDA(cudaGetLastError());
-  return MXFP4_OK;
-}
-
 int run_gather(const void* x, int64_t k_elems, const int32_t* sorted_ids, const int32_t* post, int64_t routes,
                int top_k, void* xr, int64_t cap, int sms, cudaStream_t stream) {
   const int64_t row_vecs = k_elems * 2 / 16;
