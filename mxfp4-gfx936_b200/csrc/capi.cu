@@ -157,14 +157,22 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& 
   return MXFP4_OK;
 }
 
-// Routed GEMM on CTA pairs over 256-route blocks (fused decode, 8 decode warps).
+// Fused-decode GEMM on CTA pairs (dense, or routed over 256-route blocks).
+template <int EPI>
+int fused_pair_gemm(bool fp16, const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& p, int clusters,
+                    cudaStream_t stream) {
+  if (fp16) return launch_pair<A_TMA, B_DECODE, EPI, true, 8>(ta, tb, p, clusters, stream);
+  return launch_pair<A_TMA, B_DECODE, EPI, false, 8>(ta, tb, p, clusters, stream);
+}
+
+// Routed GEMM on CTA pairs over 256-route blocks (fused decode).
 template <int AMODE, int EPI>
 int routed_pair_gemm(bool fp16, const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& p, int sms,
                      cudaStream_t stream) {
+  static_assert(AMODE == A_TMA, "routed activations are copied to routed order and loaded by TMA");
   const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
   const int clusters = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms / 2)));
-  if (fp16) return launch_pair<AMODE, B_DECODE, EPI, true, 8>(ta, tb, p, clusters, stream);
-  return launch_pair<AMODE, B_DECODE, EPI, false, 8>(ta, tb, p, clusters, stream);
+  return fused_pair_gemm<EPI>(fp16, ta, tb, p, clusters, stream);
 }
 
 // Few-token linear (M <= 256): swap-AB, K split over a cluster of `ks` CTAs.
@@ -207,14 +215,6 @@ int launch_gemv(const GemvParams& g, int sms, cudaStream_t stream) {
 }
 
 // Decode warps per CTA of the fused pair kernel (8 or 16, default 8); MXFP4_B200_DECODE_WARPS overrides.
-int decode_warps() {
-  static int v = [] {
-    const char* e = std::getenv("MXFP4_B200_DECODE_WARPS");
-    return (e && std::atoi(e) == 16) ? 16 : 8;
-  }();
-  return v;
-}
-
 int check_scales_layout(int64_t k) {
   if (k <= 0 || k % 128 != 0)
     return fail(MXFP4_ERR_INVALID_ARGUMENT, "logical K must be a positive multiple of 128, got " + std::to_string(k));
@@ -380,10 +380,17 @@ int mxfp4_dequant(const void* packed, const void* scales, void* out, int out_dty
   return MXFP4_OK;
 }
 
+// Fused mode decodes inside the GEMM producer, once per 256-row block of x.
+// From this many row blocks on, decoding each weight element once (the decode
+// kernel into an L2-resident BF16 copy, then the TMA-fed pair GEMM) costs less
+// SM time than re-decoding it per row block (measured crossover on B200: 6
+// blocks at the config-1 qkv shape, 8 at o_proj).
+constexpr int64_t kDecodeOnceRowBlocks = 6;
+
 size_t mxfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int x_dtype, int mode) {
-  (void)m;
   (void)x_dtype;
-  if (mode != MXFP4_LINEAR_SAFE) return 0;
+  const bool decode_once = mode == MXFP4_LINEAR_FUSED && (m + kP2BM - 1) / kP2BM >= kDecodeOnceRowBlocks;
+  if (mode != MXFP4_LINEAR_SAFE && !decode_once) return 0;
   return align_up(static_cast<size_t>(n) * k * 2, 256);
 }
 
@@ -514,19 +521,17 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
   const int clusters = static_cast<int>(std::min<int64_t>(tiles, info.sms / 2));
 
-  if (mode == MXFP4_LINEAR_FUSED) {
+  const size_t once_bytes = align_up(static_cast<size_t>(n) * k * 2, 256);
+  const bool decode_once = mode == MXFP4_LINEAR_FUSED && p.num_m_blocks >= kDecodeOnceRowBlocks &&
+                           ldw == k / 2 && lds == k / 32 && workspace != nullptr && workspace_bytes >= once_bytes;
+  if (mode == MXFP4_LINEAR_FUSED && !decode_once) {
     if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kP2BK / 2,
                              p.bn / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
-    if (decode_warps() == 16) {
-      if (fp16) return launch_pair<A_TMA, B_DECODE, EPI_DENSE, true, 16>(ta, tb, p, clusters, s);
-      return launch_pair<A_TMA, B_DECODE, EPI_DENSE, false, 16>(ta, tb, p, clusters, s);
-    }
-    if (fp16) return launch_pair<A_TMA, B_DECODE, EPI_DENSE, true, 8>(ta, tb, p, clusters, s);
-    return launch_pair<A_TMA, B_DECODE, EPI_DENSE, false, 8>(ta, tb, p, clusters, s);
+    return fused_pair_gemm<EPI_DENSE>(fp16, ta, tb, p, clusters, s);
   }
-  // safe: explicit dequant of W into the workspace, then the same MMA pipeline
-  const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
+  // safe (and fused with many row blocks): dequant of W into the workspace, then the same MMA pipeline
+  const size_t need = once_bytes;
   if (workspace == nullptr || workspace_bytes < need)
     return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
   MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");

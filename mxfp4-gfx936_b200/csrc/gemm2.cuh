@@ -211,6 +211,88 @@ __device__ __forceinline__ void moe_chunk(float (&v)[32], float asc, float bsc, 
   }
 }
 
+// Epilogue of one tile for one thread: accumulator row r_local (its TMEM lane)
+// of this CTA, 32-column chunks cc = grp, grp + 2, ... (two epilogue groups).
+template <int EPI>
+__device__ __forceinline__ void pair_epilogue_tile(const PairParams& p, const PairTile& c, uint32_t tbase,
+                                                   uint32_t rank, int r_local, int grp, int esz) {
+  const int pos = c.m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows + r_local;  // row of the block
+  if (EPI == EPI_DENSE) {
+    const bool row_ok = pos < p.M;
+    uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(row_ok ? pos : 0) * p.ldo * esz;
+#pragma unroll 1
+    for (int cc = grp; cc < p.bn / 32; cc += 2) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tbase + cc * 32, r);
+      tmem_ld_wait();
+      const int col0 = c.n_blk * p.bn + cc * 32;
+      if (row_ok && col0 < p.N) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if (p.bias != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = col0 + i < p.N ? col0 + i : p.N - 1;
+            v[i] = round_to(round_to(v[i], p.out_dtype) + load_weight(p.bias, p.out_dtype, col), p.out_dtype);
+          }
+        }
+        store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
+      }
+    }
+  } else if (EPI == EPI_MOE) {
+    const int route = p.sorted_ids[pos];
+    const bool row_ok = route < p.num_routes;
+    const bool scales = p.a_scale != nullptr;
+    const float asc = scales ? p.a_scale[0] : 1.0f;
+    const float bsc = scales ? p.b_scale[c.expert] : 1.0f;
+    const bool mul = p.mul_w != 0;
+    const float rw = (row_ok && mul) ? load_weight(p.topk_w, p.w_dtype, route) : 1.0f;
+    const int64_t roff = row_ok ? (static_cast<int64_t>(route / p.top_k) * p.c_stride_t +
+                                   static_cast<int64_t>(route % p.top_k) * p.c_stride_j)
+                                : 0;
+    uint8_t* orow = static_cast<uint8_t*>(p.out) + roff * esz;
+#pragma unroll 1
+    for (int cc = grp; cc < p.bn / 32; cc += 2) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tbase + cc * 32, r);
+      tmem_ld_wait();
+      const int col0 = c.n_blk * p.bn + cc * 32;
+      if (row_ok && col0 < p.N) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if (p.out_dtype == MXFP4_DTYPE_BF16) moe_chunk<MXFP4_DTYPE_BF16>(v, asc, bsc, rw, scales, mul);
+        else if (p.out_dtype == MXFP4_DTYPE_F16) moe_chunk<MXFP4_DTYPE_F16>(v, asc, bsc, rw, scales, mul);
+        else moe_chunk<MXFP4_DTYPE_F32>(v, asc, bsc, rw, scales, mul);
+        store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
+      }
+    }
+  } else {  // EPI_GLU: h = bf16(bf16(silu(bf16 g)) * bf16 u), written in routed order
+    uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(pos) * p.ldo * 2;
+#pragma unroll 1
+    for (int cc = grp; cc < p.bn / 64; cc += 2) {
+      uint32_t g[32], u[32];
+      tmem_ld_32x32b_x32(tbase + cc * 32, g);
+      tmem_ld_32x32b_x32(tbase + p.bn / 2 + cc * 32, u);
+      tmem_ld_wait();
+      const int col0 = c.n_blk * (p.bn / 2) + cc * 32;
+      if (col0 < p.glu_inter) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float gg = round_bf16(__uint_as_float(g[i]));
+          const float uu = round_bf16(__uint_as_float(u[i]));
+          const float sg = round_bf16(gg / (1.0f + expf(-gg)));
+          v[i] = round_bf16(sg * uu);
+        }
+        store_row32(orow + static_cast<int64_t>(col0) * 2, MXFP4_DTYPE_BF16, v, p.glu_inter - col0,
+                    p.vec_ok != 0);
+      }
+    }
+  }
+}
+
 template <int AMODE, int BMODE, int EPI, bool FP16, int DECODE_WARPS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECODE_WARPS>::kThreads, 1)
     mxfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -396,81 +478,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
       if (!mbar_wait_cluster(&tfull[acc], (tl >> 1) & 1, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
-      const int pos = c.m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows + r_local;  // row of the block
-      if (EPI == EPI_DENSE) {
-        const bool row_ok = pos < p.M;
-        uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(row_ok ? pos : 0) * p.ldo * esz;
-#pragma unroll 1
-        for (int cc = grp; cc < p.bn / 32; cc += 2) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + cc * 32, r);
-          tmem_ld_wait();
-          const int col0 = c.n_blk * p.bn + cc * 32;
-          if (row_ok && col0 < p.N) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            if (p.bias != nullptr) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int col = col0 + i < p.N ? col0 + i : p.N - 1;
-                v[i] = round_to(round_to(v[i], p.out_dtype) + load_weight(p.bias, p.out_dtype, col), p.out_dtype);
-              }
-            }
-            store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
-          }
-        }
-      } else if (EPI == EPI_MOE) {
-        const int route = p.sorted_ids[pos];
-        const bool row_ok = route < p.num_routes;
-        const bool scales = p.a_scale != nullptr;
-        const float asc = scales ? p.a_scale[0] : 1.0f;
-        const float bsc = scales ? p.b_scale[c.expert] : 1.0f;
-        const bool mul = p.mul_w != 0;
-        const float rw = (row_ok && mul) ? load_weight(p.topk_w, p.w_dtype, route) : 1.0f;
-        const int64_t roff = row_ok ? (static_cast<int64_t>(route / p.top_k) * p.c_stride_t +
-                                       static_cast<int64_t>(route % p.top_k) * p.c_stride_j)
-                                    : 0;
-        uint8_t* orow = static_cast<uint8_t*>(p.out) + roff * esz;
-#pragma unroll 1
-        for (int cc = grp; cc < p.bn / 32; cc += 2) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + cc * 32, r);
-          tmem_ld_wait();
-          const int col0 = c.n_blk * p.bn + cc * 32;
-          if (row_ok && col0 < p.N) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            if (p.out_dtype == MXFP4_DTYPE_BF16) moe_chunk<MXFP4_DTYPE_BF16>(v, asc, bsc, rw, scales, mul);
-            else if (p.out_dtype == MXFP4_DTYPE_F16) moe_chunk<MXFP4_DTYPE_F16>(v, asc, bsc, rw, scales, mul);
-            else moe_chunk<MXFP4_DTYPE_F32>(v, asc, bsc, rw, scales, mul);
-            store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
-          }
-        }
-      } else {  // EPI_GLU: h = bf16(bf16(silu(bf16 g)) * bf16 u), written in routed order
-        uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(pos) * p.ldo * 2;
-#pragma unroll 1
-        for (int cc = grp; cc < p.bn / 64; cc += 2) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(tbase + cc * 32, g);
-          tmem_ld_32x32b_x32(tbase + p.bn / 2 + cc * 32, u);
-          tmem_ld_wait();
-          const int col0 = c.n_blk * (p.bn / 2) + cc * 32;
-          if (col0 < p.glu_inter) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float gg = round_bf16(__uint_as_float(g[i]));
-              const float uu = round_bf16(__uint_as_float(u[i]));
-              const float sg = round_bf16(gg / (1.0f + expf(-gg)));
-              v[i] = round_bf16(sg * uu);
-            }
-            store_row32(orow + static_cast<int64_t>(col0) * 2, MXFP4_DTYPE_BF16, v, p.glu_inter - col0,
-                        p.vec_ok != 0);
-          }
-        }
-      }
+      pair_epilogue_tile<EPI>(p, c, tbase, rank, r_local, grp, esz);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);

@@ -47,7 +47,9 @@ def test_matches_reference_golden(monkeypatch, backend, case):
 
 
 SHAPES = [(1, 64, 128), (8, 64, 128), (16, 256, 2048), (64, 5120, 2048), (130, 384, 256),
-          (370, 512, 2048), (300, 1000, 512), (257, 2048, 4096)]
+          (370, 512, 2048), (300, 1000, 512), (257, 2048, 4096),
+          # four-CTA kernel (>= 4 row blocks of 256): odd row-block count, ragged N, K shorter than the ring
+          (1100, 1000, 512), (1024, 640, 1024), (2048, 2048, 256)]
 
 
 @pytest.mark.parametrize("m,n,k", SHAPES)
@@ -126,3 +128,36 @@ def test_full_size_against_torch_reference(monkeypatch, name, m, n, k):
     exact = gref.linear(x.float(), w, s)
     assert (fused.float() - exact).abs().max().item() <= 2 * ulp.item()
     assert soft.device_status() == 0
+
+
+@pytest.mark.parametrize("backend", ["safe", "fused"])
+def test_bias_many_row_blocks(monkeypatch, backend):
+    x, w, s = _inputs(1100, 480, 1024, seed=21)
+    bias = torch.randn(480).to(torch.bfloat16)
+    y = _run(monkeypatch, backend, x.cuda(), w.cuda(), s.cuda(), bias.cuda())
+    ref = O.linear(_np(x), "bf16", w.numpy(), s.numpy(), _np(bias))
+    ok, err, bound, rel = O.check_close(_np(y), ref)
+    assert ok, (err, bound, rel)
+
+
+def test_fused_repeatable_full_size(monkeypatch):
+    # the fused kernels exchange decoded weights between CTAs: repeated runs must agree bit for bit
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(4096, 2048, generator=g, device="cuda").to(torch.bfloat16)
+    w = torch.randint(0, 256, (5120, 1024), generator=g, device="cuda", dtype=torch.uint8)
+    s = torch.randint(118, 131, (5120, 64), generator=g, device="cuda", dtype=torch.uint8)
+    first = _run(monkeypatch, "fused", x, w, s)
+    for _ in range(3):
+        assert torch.equal(_run(monkeypatch, "fused", x, w, s).view(torch.int16), first.view(torch.int16))
+    assert soft.device_status() == 0
+
+
+def test_fused_many_row_blocks_strided_weights(monkeypatch):
+    # >= 6 row blocks with a weight view that is not contiguous: the fused mode
+    # cannot use its decode-once copy and decodes inside the GEMM instead
+    x, w, s = _inputs(1600, 384, 512, seed=33)
+    wide = torch.cat([w, w], dim=1)
+    y = _run(monkeypatch, "fused", x.cuda(), wide[:, :256].cuda(), s.cuda())
+    ref = O.linear(_np(x), "bf16", w.numpy(), s.numpy())
+    ok, err, bound, rel = O.check_close(_np(y), ref)
+    assert ok, (err, bound, rel)
