@@ -4,9 +4,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 Headline workload (the large-prefill dense linear):
-qkv_proj M=4096, K=2048, N=5120 through the fused W4A16 kernel (weights
-decoded inside the GEMM producer).  A "step" is one pass of the linear over
-one batch.  ``value`` is the whole-job TFLOP/s (2*M*N*K per step) with the
+qkv_proj M=4096, K=2048, N=5120 through the fused W4A16 backend.  With 16
+row blocks of 256 it decodes each weight element once (the decode kernel
+into an L2-resident BF16 copy, then the TMA-fed pair GEMM: two launches per
+step); ``roofline`` is the GEMM's, from the step time minus the separately
+timed decode kernel.  A "step" is one pass of the linear over one batch.  ``value`` is the whole-job TFLOP/s (2*M*N*K per step) with the
 inputs resident in HBM, timed with CUDA events on the launching stream over
 exactly K steps (CUDA-graph replays rotating 4 input sets of 64 MB each, so
 the working set of consecutive steps exceeds the 126 MB L2).  ``e2e`` times the
@@ -236,6 +238,20 @@ def bench_linear(soft, shape, steps, warmup, n_sets, backend, device, sampler=No
     return ms
 
 
+def bench_decode_kernel(soft, shape, steps, warmup, device):
+    """The weight decode kernel alone (the first of the two launches of a
+    decode-once fused linear), same rotation of 4 weight sets."""
+    m, n, k = shape
+    sets = [make_linear_inputs(1, n, k, i, device)[1:] for i in range(4)]
+    gs = graphs_for(lambda w, s: soft.dequant_mxfp4(w, s, torch.bfloat16), sets, torch.cuda.Stream())
+    ms = time_graphs(gs, steps, warmup)
+    del gs, sets
+    return ms
+
+
+DECODE_ONCE_ROW_BLOCKS = 6  # mirrors kDecodeOnceRowBlocks in csrc/capi.cu
+
+
 def bench_e2e_linear(soft, shape, steps, warmup, device):
     m, n, k = shape
     set_backend("fused")
@@ -393,6 +409,11 @@ def main():
     ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "fused", device, sampler=sampler)
     flops = 2.0 * m * n * k
     tflops = flops / (ms * 1e-3) / 1e12
+    # decode-once (>= 6 row blocks): two launches per step, the decode kernel then the GEMM
+    decode_once = (m + 255) // 256 >= DECODE_ONCE_ROW_BLOCKS
+    dec_ms = bench_decode_kernel(soft, QKV, args.steps, args.warmup, device) if decode_once else 0.0
+    gemm_ms = ms - dec_ms
+    gemm_tflops = flops / (gemm_ms * 1e-3) / 1e12
     e2e_ms, h2d, d2h = bench_e2e_linear(soft, QKV, max(10, args.steps // 4), args.warmup, device)
 
     line = {
@@ -402,12 +423,16 @@ def main():
         "config": {"workload": "config1_qkv_prefill", "M": m, "N": n, "K": k, "backend": "fused",
                    "l2": "4 rotating input sets of 64 MB (working set > 126 MB L2)", "timing": "CUDA graph of the 4-set rotation replayed, CUDA events",
                    "parallelism": "single GPU"},
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": tflops / pk["bf16_tflops"], "traffic": profile_traffic("linear_fused_qkv"),
-                     "peak_source": f"{pk_kind} bf16 burst"},
+        "roofline": {"bound": "tensor", "achieved": gemm_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": gemm_tflops / pk["bf16_tflops"], "traffic": profile_traffic("linear_fused_qkv"),
+                     "peak_source": f"{pk_kind} bf16 burst",
+                     "kernel": "pair GEMM (TMA-fed decoded weights)" if decode_once else "pair GEMM (decode in producer)",
+                     "kernel_ms": gemm_ms, "decode_kernel_ms": dec_ms,
+                     "decode_kernel_gbs": (n * k // 2 + n * k // 32 + 2 * n * k) / (dec_ms * 1e6) if dec_ms else None,
+                     "step_frac": tflops / pk["bf16_tflops"]},
         "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if decode_once else 1),
         "clocks": sampler.result(),
     }
 
@@ -517,17 +542,21 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
     m, n, k = QKV
     set_backend("fused")
     barrier = lambda: dist.barrier(device_ids=[device.index])  # noqa: E731
-    sets, shard_sets = [], []
+    sets, shard_sets, nccl_sets = [], [], []
     for i in range(4):
         x, w, s = make_linear_inputs(m, n, k, i, device)  # same full weight on every rank
-        layer = cp.ColumnParallelLinear.from_full(w, s, rank, world)
+        layer = cp.ColumnParallelLinear.from_full(w, s, rank, world, fused=True)
         sets.append((x, layer))
         shard_sets.append((x, layer.w, layer.s))
+        nccl_sets.append((x, cp.ColumnParallelLinear(layer.w, layer.s, n, rank, world)))
         del w, s
     # the shard GEMM alone (the dominant kernel), then GEMM + all-gather
     gs_local = graphs_for(lambda x, w, s: soft.linear_mxfp4_soft(x, w, s), shard_sets, torch.cuda.Stream())
     ms_gemm = _max_over_ranks(time_graphs(gs_local, args.steps, args.warmup, barrier=barrier), device)
     del gs_local
+    gs = graphs_for(lambda x, layer: layer(x), nccl_sets, torch.cuda.Stream())
+    ms_nccl = _max_over_ranks(time_graphs(gs, args.steps, args.warmup, barrier=barrier), device)
+    del gs, nccl_sets
     gs = graphs_for(lambda x, layer: layer(x), sets, torch.cuda.Stream())
     sampler = ClockSampler(device.index)
     ms = _max_over_ranks(time_graphs(gs, args.steps, args.warmup, barrier=barrier, sampler=sampler), device)
@@ -582,7 +611,8 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE config-1 distributions, seeded)",
             "config": {"workload": "config1_qkv_prefill", "M": m, "N": n, "K": k, "backend": "fused",
-                       "parallelism": f"tp{world}: column-sharded W (N/{world} rows per GPU) + NCCL all-gather",
+                       "parallelism": f"tp{world}: column-sharded W (N/{world} rows per GPU), all-gather fused "
+                                      "into the GEMM epilogue (peer stores over NVLink) + device barrier",
                        "l2": "4 rotating input sets of 64 MB (working set > 126 MB L2)",
                        "timing": "CUDA graph of the 4-set rotation replayed, CUDA events, max over ranks"},
             "roofline": {"bound": "tensor", "achieved": gemm_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
@@ -595,9 +625,11 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
                               "shard_gemm_ms": ms_gemm},
             "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * 3,
             "clocks": sampler.result(),
-            "extra": {"config2_moe_layer_ep": {
+            "extra": {"tp_nccl_allgather": {"ms": ms_nccl, "tflops": flops / (ms_nccl * 1e-3) / 1e12,
+                                            "what": "shard GEMM then NCCL all_gather_into_tensor + interleave"},
+                      "config2_moe_layer_ep": {
                 "ms": ms_ep, "tokens_per_s": MOE["t"] / (ms_ep * 1e-3), "tflops": fm / ms_ep / 1e9,
                 "experts_per_gpu": MOE["e"] // world, "tokens_per_gpu": MOE["t"] // world,
                 "roofline_target_ms": t_ep_roof * 1e3, "roofline_frac": t_ep_roof * 1e3 / ms_ep,

@@ -192,6 +192,44 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
                     int top_k, int num_experts, int64_t hidden, int64_t inter, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Multi-GPU dense linear (column-sharded).  No counterpart in    */
+/* the reference; replaces the shard GEMM + NCCL all-gather pair.           */
+/* mxfp4_linear_w4a16 whose output block is also written, from the GEMM     */
+/* epilogue, into the buffers of up to 7 other ranks on this node: `out` is */
+/* this rank's [m, n] column block inside its full [m, n * world] output    */
+/* (row stride ldo elements), peer_out[j] the same block inside rank j's    */
+/* output, mapped into this process (CUDA IPC over NVLink).  A host array   */
+/* of num_peers device pointers, 16-byte aligned for the vector stores.     */
+/* Arguments otherwise as mxfp4_linear_w4a16.  The peers' buffers hold the  */
+/* block once every rank has passed mxfp4_peer_barrier after this call.     */
+int mxfp4_linear_w4a16_allgather(const void* x, int x_dtype, int64_t ldx, const void* w_packed,
+                                 int64_t ldw, const void* w_scales, int64_t lds, const void* bias,
+                                 void* out, void* const* peer_out, int num_peers, int64_t ldo,
+                                 int64_t m, int64_t n, int64_t k, int mode, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* Peer-mapped buffers for the multi-GPU paths (CUDA IPC; one process per   */
+/* GPU on one node).  mxfp4_ipc_alloc: zero-filled device allocation of the  */
+/* current device and its 64-byte IPC handle (written to `handle`).         */
+/* mxfp4_ipc_open: maps another process's allocation into the current       */
+/* device's context with peer access enabled; mxfp4_ipc_close unmaps it,    */
+/* mxfp4_ipc_free releases a local allocation once every peer closed it.   */
+int mxfp4_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int mxfp4_ipc_open(const void* handle, void** ptr);
+int mxfp4_ipc_close(void* ptr);
+int mxfp4_ipc_free(void* ptr);
+
+/* Device-side barrier of `world` ranks (one kernel, one warp).  flags: a    */
+/* host array of `world` device pointers, flags[j] = rank j's int32 flag    */
+/* array [world] mapped into this process (flags[rank] is the local one);   */
+/* all flag arrays start at zero.  counter: a local device int32, zero     */
+/* before the first call, advanced by one per call.  Orders this rank's     */
+/* earlier stores (including stores into peers' memory) before the signal.  */
+/* Every rank makes the same sequence of calls.  A wait longer than about   */
+/* 2 s records MXFP4_ERR_TIMEOUT in the device status word and returns.     */
+int mxfp4_peer_barrier(int32_t* const* flags, int rank, int world, int32_t* counter, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

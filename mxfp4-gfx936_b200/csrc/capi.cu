@@ -125,6 +125,11 @@ int elem_size(int dtype) {
   return 0;
 }
 
+struct PeerOut {
+  int n = 0;
+  void* p[kMaxPeers] = {};
+};
+
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 constexpr int64_t kSmallMaxRows = 256;  // token counts served by the split-K few-token kernel
@@ -141,11 +146,11 @@ int run_gather(const void* x, int64_t k_elems, const int32_t* sorted_ids, const 
   return MXFP4_OK;
 }
 
-template <int AMODE, int BMODE, int EPI, bool FP16, int DW>
+template <int AMODE, int BMODE, int EPI, bool FP16, int DW, bool PEERS = false>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& p, int clusters,
                 cudaStream_t stream) {
-  using Cfg = Pair2Cfg<BMODE, DW>;
-  auto kern = mxfp4_gemm_pair_kernel<AMODE, BMODE, EPI, FP16, DW>;
+  using Cfg = Pair2Cfg<BMODE, DW, PEERS>;
+  auto kern = mxfp4_gemm_pair_kernel<AMODE, BMODE, EPI, FP16, DW, PEERS>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -394,10 +399,39 @@ size_t mxfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int x_dtype,
   return align_up(static_cast<size_t>(n) * k * 2, 256);
 }
 
-int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw,
-                       const void* w_scales, int64_t lds, const void* bias, void* out, int64_t ldo,
-                       int64_t m, int64_t n, int64_t k, int mode, void* workspace,
-                       size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Copy the [m, n] block at `out` (row stride ldo) into every peer buffer at the
+// same offset: the all-gather of the few-token paths, whose kernels have no
+// peer-store epilogue.
+__global__ void __launch_bounds__(256) push_rows_kernel(const uint8_t* __restrict__ src, int64_t m,
+                                                        int64_t row_bytes, int64_t ld_bytes, PeerOut peers) {
+  const bool vec = (row_bytes % 16 == 0) && (ld_bytes % 16 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0);
+  const int64_t units = vec ? row_bytes / 16 : row_bytes / 2;
+  const int64_t total = m * units;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / units, u = i % units;
+    const int64_t off = r * ld_bytes + u * (vec ? 16 : 2);
+    if (vec) {
+      const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+#pragma unroll
+      for (int j = 0; j < kMaxPeers; ++j)
+        if (j < peers.n) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.p[j]) + off) = v;
+    } else {
+      const uint16_t v = *reinterpret_cast<const uint16_t*>(src + off);
+#pragma unroll
+      for (int j = 0; j < kMaxPeers; ++j)
+        if (j < peers.n) *reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(peers.p[j]) + off) = v;
+    }
+  }
+}
+
+int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw, const void* w_scales,
+                int64_t lds, const void* bias, void* out, int64_t ldo, int64_t m, int64_t n, int64_t k, int mode,
+                void* workspace, size_t workspace_bytes, void* stream, const PeerOut& peers) {
   DevInfo info;
   if (int rc = current_device_info(info)) return rc;
   MX_CHECK(x && w_packed && w_scales && out, "null pointer");
@@ -410,6 +444,15 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   MX_CHECK(aligned(w_scales, 4) && lds % 4 == 0, "scales must be 4-byte aligned rows");
   if (m == 0) return MXFP4_OK;
   cudaStream_t s = as_stream(stream);
+  auto push = [&](int rc) -> int {
+    if (rc != MXFP4_OK || peers.n == 0 || m == 0) return rc;
+    const int64_t esz = 2;
+    const int64_t total = m * n;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 2047) / 2048, info.sms * 4)));
+    push_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(out), m, n * esz, ldo * esz, peers);
+    MX_CUDA(cudaGetLastError());
+    return MXFP4_OK;
+  };
   const bool fp16 = x_dtype == MXFP4_DTYPE_F16;
   const CUtensorMapDataType xt = fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 
@@ -431,8 +474,8 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
       g.ldw = ldw;
       g.w_scales = static_cast<const uint8_t*>(w_scales);
       g.lds = lds;
-      if (fp16) return launch_gemv<B_DECODE, true>(g, info.sms, s);
-      return launch_gemv<B_DECODE, false>(g, info.sms, s);
+      if (fp16) return push(launch_gemv<B_DECODE, true>(g, info.sms, s));
+      return push(launch_gemv<B_DECODE, false>(g, info.sms, s));
     }
     const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
     if (workspace == nullptr || workspace_bytes < need)
@@ -441,8 +484,8 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
     if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
     g.w = static_cast<const uint8_t*>(workspace);
     g.ldw = k * 2;
-    if (fp16) return launch_gemv<B_TMA, true>(g, info.sms, s);
-    return launch_gemv<B_TMA, false>(g, info.sms, s);
+    if (fp16) return push(launch_gemv<B_TMA, true>(g, info.sms, s));
+    return push(launch_gemv<B_TMA, false>(g, info.sms, s));
   }
   if (m <= kSmallMaxRows) {
     SmallParams q{};
@@ -472,8 +515,8 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
       if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kSmBK / 2, kSmRows,
                                CU_TENSOR_MAP_SWIZZLE_NONE))
         return rc;
-      if (fp16) return launch_small<B_DECODE, true>(ta, tb, q, s);
-      return launch_small<B_DECODE, false>(ta, tb, q, s);
+      if (fp16) return push(launch_small<B_DECODE, true>(ta, tb, q, s));
+      return push(launch_small<B_DECODE, false>(ta, tb, q, s));
     }
     const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
     if (workspace == nullptr || workspace_bytes < need)
@@ -482,8 +525,8 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
     if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
     if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kSmBK, kSmRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
-    if (fp16) return launch_small<B_TMA, true>(ta, tb, q, s);
-    return launch_small<B_TMA, false>(ta, tb, q, s);
+    if (fp16) return push(launch_small<B_TMA, true>(ta, tb, q, s));
+    return push(launch_small<B_TMA, false>(ta, tb, q, s));
   }
   if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
 
@@ -518,6 +561,13 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   p.out_dtype = x_dtype;
   p.bias = bias;
   p.vec_ok = aligned(out, 16) && (ldo * 2) % 16 == 0;
+  p.num_peers = peers.n;
+  for (int j = 0; j < kMaxPeers; ++j) p.peer_out[j] = j < peers.n ? peers.p[j] : nullptr;
+  if (peers.n > 0) {
+    bool peers_aligned = true;
+    for (int j = 0; j < peers.n; ++j) peers_aligned = peers_aligned && aligned(peers.p[j], 16);
+    p.vec_ok = p.vec_ok && peers_aligned;
+  }
   const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
   const int clusters = static_cast<int>(std::min<int64_t>(tiles, info.sms / 2));
 
@@ -528,6 +578,10 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
     if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kP2BK / 2,
                              p.bn / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
+    if (peers.n > 0) {
+      if (fp16) return launch_pair<A_TMA, B_DECODE, EPI_DENSE, true, 8, true>(ta, tb, p, clusters, s);
+      return launch_pair<A_TMA, B_DECODE, EPI_DENSE, false, 8, true>(ta, tb, p, clusters, s);
+    }
     return fused_pair_gemm<EPI_DENSE>(fp16, ta, tb, p, clusters, s);
   }
   // safe (and fused with many row blocks): dequant of W into the workspace, then the same MMA pipeline
@@ -538,8 +592,129 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
   if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
   if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kP2BK, p.bn / 2, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
+  if (peers.n > 0) {
+    if (fp16) return launch_pair<A_TMA, B_TMA, EPI_DENSE, true, 0, true>(ta, tb, p, clusters, s);
+    return launch_pair<A_TMA, B_TMA, EPI_DENSE, false, 0, true>(ta, tb, p, clusters, s);
+  }
   if (fp16) return launch_pair<A_TMA, B_TMA, EPI_DENSE, true, 0>(ta, tb, p, clusters, s);
   return launch_pair<A_TMA, B_TMA, EPI_DENSE, false, 0>(ta, tb, p, clusters, s);
+}
+
+
+// Device-side barrier over peer-mapped flag arrays (one warp): lane j signals
+// rank j and waits for rank j's signal.  Every rank calls it the same number
+// of times; the epoch is the local call count, kept on the device so the
+// barrier works inside CUDA graphs.
+struct PeerFlags {
+  int32_t* f[kMaxPeers + 1];  // flag array [world] of each rank
+};
+
+__global__ void peer_barrier_kernel(PeerFlags flags, int rank, int world, int32_t* counter) {
+  const int lane = threadIdx.x;
+  int epoch = 0;
+  if (lane == 0) {
+    epoch = *counter + 1;
+    *counter = epoch;
+  }
+  epoch = __shfl_sync(0xFFFFFFFFu, epoch, 0);
+  asm volatile("fence.acq_rel.sys;" ::: "memory");  // this rank's earlier (peer) stores before the signal
+  if (lane < world) asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flags.f[lane] + rank), "r"(epoch) : "memory");
+  if (lane < world) {
+    const int32_t* mine = flags.f[rank] + lane;
+    const long long t0 = clock64();
+    while (true) {
+      int32_t v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (v - epoch >= 0) break;
+      if (clock64() - t0 > kWaitCycles) {
+        record_error(MXFP4_ERR_TIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncwarp();
+}
+
+}  // namespace
+
+extern "C" {
+
+int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw,
+                       const void* w_scales, int64_t lds, const void* bias, void* out, int64_t ldo,
+                       int64_t m, int64_t n, int64_t k, int mode, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return linear_impl(x, x_dtype, ldx, w_packed, ldw, w_scales, lds, bias, out, ldo, m, n, k, mode, workspace,
+                     workspace_bytes, stream, PeerOut{});
+}
+
+int mxfp4_linear_w4a16_allgather(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw,
+                                 const void* w_scales, int64_t lds, const void* bias, void* out,
+                                 void* const* peer_out, int num_peers, int64_t ldo, int64_t m, int64_t n,
+                                 int64_t k, int mode, void* workspace, size_t workspace_bytes, void* stream) {
+  MX_CHECK(num_peers >= 0 && num_peers <= kMaxPeers, "num_peers must be in [0, 7]");
+  MX_CHECK(num_peers == 0 || peer_out != nullptr, "null peer_out");
+  PeerOut peers{};
+  peers.n = num_peers;
+  for (int j = 0; j < num_peers; ++j) {
+    MX_CHECK(peer_out[j] != nullptr, "null peer output pointer");
+    peers.p[j] = peer_out[j];
+  }
+  return linear_impl(x, x_dtype, ldx, w_packed, ldw, w_scales, lds, bias, out, ldo, m, n, k, mode, workspace,
+                     workspace_bytes, stream, peers);
+}
+
+int mxfp4_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(ptr != nullptr && handle != nullptr && bytes > 0, "bad ipc_alloc arguments");
+  void* p = nullptr;
+  MX_CUDA(cudaMalloc(&p, bytes));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(MXFP4_ERR_CUDA, std::string("ipc_alloc: ") + cudaGetErrorString(e));
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return MXFP4_OK;
+}
+
+int mxfp4_ipc_open(const void* handle, void** ptr) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(ptr != nullptr && handle != nullptr, "bad ipc_open arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  MX_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MXFP4_OK;
+}
+
+int mxfp4_ipc_close(void* ptr) {
+  MX_CUDA(cudaIpcCloseMemHandle(ptr));
+  return MXFP4_OK;
+}
+
+int mxfp4_ipc_free(void* ptr) {
+  MX_CUDA(cudaFree(ptr));
+  return MXFP4_OK;
+}
+
+int mxfp4_peer_barrier(int32_t* const* flags, int rank, int world, int32_t* counter, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(world >= 1 && world <= kMaxPeers + 1 && rank >= 0 && rank < world, "bad rank/world");
+  MX_CHECK(flags != nullptr && counter != nullptr, "null pointer");
+  PeerFlags f{};
+  for (int j = 0; j < world; ++j) {
+    MX_CHECK(flags[j] != nullptr && aligned(flags[j], 4), "flag arrays must be non-null and 4-byte aligned");
+    f.f[j] = flags[j];
+  }
+  peer_barrier_kernel<<<1, 32, 0, as_stream(stream)>>>(f, rank, world, counter);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
 }
 
 int64_t mxfp4_moe_route_capacity(int64_t num_routes, int num_experts, int block_m) {

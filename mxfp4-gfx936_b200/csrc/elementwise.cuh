@@ -10,38 +10,46 @@
 namespace mx {
 
 // ---------------------------------------------------------------------------
-// K0: one thread per 32-element block (16 packed bytes + 1 scale byte).
+// Dequant: a thread decodes one 32-bit packed word (8 values) per step, and
+// the 32 lanes of a warp take 32 consecutive words, so every load (128 B of
+// packed codes) and every store (512 B of BF16/FP16, 1 KB of FP32) of the warp
+// is one contiguous segment.  Each thread walks 4 words spaced one warp-width
+// apart per iteration for memory-level parallelism.
 // ---------------------------------------------------------------------------
 template <int OUT>
 __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ packed,
                                                       const uint8_t* __restrict__ scales,
                                                       void* __restrict__ out, int64_t num_blocks) {
-  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < num_blocks;
-       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint4 q = *reinterpret_cast<const uint4*>(packed + b * 16);
-    const uint32_t code = scales[b];
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    if (OUT == MXFP4_DTYPE_BF16) {
-      const uint32_t sc = e8m0_to_bf16x2(code);
-      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + b * 32);
+  const int64_t num_words = num_blocks * 4;  // 4 words of 8 codes per 32-value scale block
+  const uint32_t* words = reinterpret_cast<const uint32_t*>(packed);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t warps_total = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t base = warp_global * 128; base < num_words; base += warps_total * 128) {
+    uint32_t w[4], code[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = decode8_bf16(w[i], sc);
-    } else if (OUT == MXFP4_DTYPE_F16) {
-      const float sc = e8m0_to_f32(code);
-      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + b * 32);
+    for (int i = 0; i < 4; ++i) {
+      const int64_t wi = base + lane + 32 * i;
+      w[i] = wi < num_words ? __ldg(words + wi) : 0u;
+      code[i] = wi < num_words ? __ldg(scales + (wi >> 2)) : 127u;
+    }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = decode8_f16(w[i], sc);
-    } else {
-      const float sc = e8m0_to_f32(code);
-      float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + b * 32);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 4; ++i) {
+      const int64_t wi = base + lane + 32 * i;
+      if (wi >= num_words) break;
+      if (OUT == MXFP4_DTYPE_BF16) {
+        reinterpret_cast<uint4*>(out)[wi] = decode8_bf16(w[i], e8m0_to_bf16x2(code[i]));
+      } else if (OUT == MXFP4_DTYPE_F16) {
+        reinterpret_cast<uint4*>(out)[wi] = decode8_f16(w[i], e8m0_to_f32(code[i]));
+      } else {
+        const float sc = e8m0_to_f32(code[i]);
         uint32_t v[4];
         e2m1x8_to_bf16x8(w[i], v);
-        o[2 * i] = make_float4(__uint_as_float(v[0] << 16) * sc, __uint_as_float(v[0] & 0xFFFF0000u) * sc,
-                               __uint_as_float(v[1] << 16) * sc, __uint_as_float(v[1] & 0xFFFF0000u) * sc);
-        o[2 * i + 1] = make_float4(__uint_as_float(v[2] << 16) * sc, __uint_as_float(v[2] & 0xFFFF0000u) * sc,
-                                   __uint_as_float(v[3] << 16) * sc, __uint_as_float(v[3] & 0xFFFF0000u) * sc);
+        float4* o = reinterpret_cast<float4*>(out) + 2 * wi;
+        o[0] = make_float4(__uint_as_float(v[0] << 16) * sc, __uint_as_float(v[0] & 0xFFFF0000u) * sc,
+                           __uint_as_float(v[1] << 16) * sc, __uint_as_float(v[1] & 0xFFFF0000u) * sc);
+        o[1] = make_float4(__uint_as_float(v[2] << 16) * sc, __uint_as_float(v[2] & 0xFFFF0000u) * sc,
+                           __uint_as_float(v[3] << 16) * sc, __uint_as_float(v[3] & 0xFFFF0000u) * sc);
       }
     }
   }

@@ -31,9 +31,13 @@ constexpr int kP2ABytes = kP2HalfRows * kP2BK * 2;    // 16 KB
 constexpr int kP2BBytes = kP2HalfRows * kP2BK * 2;    // 16 KB
 constexpr int kP2PBytes = kP2HalfRows * kP2BK / 2;    // 4 KB
 
-template <int BMODE, int DECODE_WARPS>
+// PEERS: the dense epilogue also stores into other ranks' buffers; it stages
+// each warp's 32 x 32 output chunk in shared memory (2 KB per epilogue warp)
+// so that every global store of the warp covers whole 64-byte row segments,
+// the unit that crosses NVLink efficiently.
+template <int BMODE, int DECODE_WARPS, bool PEERS = false>
 struct Pair2Cfg {
-  static constexpr int kStages = 6;
+  static constexpr int kStages = (BMODE == B_DECODE && PEERS) ? 5 : 6;
   static constexpr int kDecodeWarps = BMODE == B_DECODE ? DECODE_WARPS : 0;
   // warps 0-3 control, 4-7 epilogue group 0, then the decoders, then epilogue group 1
   static constexpr int kEpi1Warp = 8 + kDecodeWarps;
@@ -41,7 +45,8 @@ struct Pair2Cfg {
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kP2ABytes;
   static constexpr int kOffP = kOffB + kStages * kP2BBytes;
-  static constexpr int kOffBar = kOffP + (BMODE == B_DECODE ? kStages * kP2PBytes : 0);
+  static constexpr int kOffOut = kOffP + (BMODE == B_DECODE ? kStages * kP2PBytes : 0);
+  static constexpr int kOffBar = kOffOut + (PEERS ? 8 * 2048 : 0);
   // full, ready, empty per stage; tfull[2], tempty[2], drain
   static constexpr int kNumBars = 3 * kStages + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
@@ -122,6 +127,8 @@ __device__ __forceinline__ void umma2_commit_mc(uint64_t* bar, uint16_t mask) {
       : "memory");
 }
 
+constexpr int kMaxPeers = 7;  // up to 8 ranks per node
+
 struct PairParams {
   int M, N, K;                     // dense: rows of A; N: output columns (GLU: 2*inter); K: reduction
   int bn;                          // tile width: multiple of 32, <= 256 (each CTA holds bn/2 weight rows)
@@ -153,6 +160,12 @@ struct PairParams {
   int mul_w;
   int64_t c_stride_t, c_stride_j;  // routed C row offset, elements
   int vec_ok;
+  // dense all-gather epilogue: every output chunk is also stored, at the same
+  // offset, into the buffers of num_peers other ranks (peer_out[j] is the
+  // peer's mapping of its output over NVLink, already offset to this rank's
+  // columns; ldo is the full row stride)
+  int num_peers;
+  void* peer_out[kMaxPeers];
 };
 using DenseParams = PairParams;
 
@@ -213,12 +226,14 @@ __device__ __forceinline__ void moe_chunk(float (&v)[32], float asc, float bsc, 
 
 // Epilogue of one tile for one thread: accumulator row r_local (its TMEM lane)
 // of this CTA, 32-column chunks cc = grp, grp + 2, ... (two epilogue groups).
-template <int EPI>
+template <int EPI, bool PEERS = false>
 __device__ __forceinline__ void pair_epilogue_tile(const PairParams& p, const PairTile& c, uint32_t tbase,
-                                                   uint32_t rank, int r_local, int grp, int esz) {
+                                                   uint32_t rank, int r_local, int grp, int esz,
+                                                   uint32_t stage = 0) {
   const int pos = c.m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows + r_local;  // row of the block
   if (EPI == EPI_DENSE) {
     const bool row_ok = pos < p.M;
+    const int lane = r_local & 31;
     uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<int64_t>(row_ok ? pos : 0) * p.ldo * esz;
 #pragma unroll 1
     for (int cc = grp; cc < p.bn / 32; cc += 2) {
@@ -226,19 +241,58 @@ __device__ __forceinline__ void pair_epilogue_tile(const PairParams& p, const Pa
       tmem_ld_32x32b_x32(tbase + cc * 32, r);
       tmem_ld_wait();
       const int col0 = c.n_blk * p.bn + cc * 32;
-      if (row_ok && col0 < p.N) {
-        float v[32];
+      if (col0 >= p.N) continue;  // warp-uniform
+      float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        if (p.bias != nullptr) {
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (p.bias != nullptr) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = col0 + i < p.N ? col0 + i : p.N - 1;
-            v[i] = round_to(round_to(v[i], p.out_dtype) + load_weight(p.bias, p.out_dtype, col), p.out_dtype);
-          }
+        for (int i = 0; i < 32; ++i) {
+          const int col = col0 + i < p.N ? col0 + i : p.N - 1;
+          v[i] = round_to(round_to(v[i], p.out_dtype) + load_weight(p.bias, p.out_dtype, col), p.out_dtype);
         }
-        store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
       }
+      if constexpr (PEERS) {
+        if (p.out_dtype != MXFP4_DTYPE_F32 && p.vec_ok && col0 + 32 <= p.N) {
+          // stage the warp's 32 rows x 64 B, then store whole 64-byte row
+          // segments (4 lanes per row, 8 rows per instruction) locally and to
+          // every peer; chunk c of row r sits at c ^ ((r >> 1) & 3) (no bank conflicts)
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = p.out_dtype == MXFP4_DTYPE_BF16 ? f32x2_to_bf16x2(v[2 * i], v[2 * i + 1])
+                                                    : f32x2_to_f16x2(v[2 * i], v[2 * i + 1]);
+          const uint32_t xs = (lane >> 1) & 3;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            st_shared_v4(stage + lane * 64 + ((q4 ^ xs) << 4),
+                         make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]));
+          __syncwarp();
+          const int row0 = pos - lane;  // first row of this warp
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rr = 8 * i + (lane >> 2);
+            const int ch = lane & 3;
+            const uint4 val = ld_shared_v4(stage + rr * 64 + ((ch ^ ((rr >> 1) & 3)) << 4));
+            if (row0 + rr < p.M) {
+              const int64_t off = (static_cast<int64_t>(row0 + rr) * p.ldo + col0 + ch * 8) * 2;
+              *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + off) = val;
+#pragma unroll
+              for (int j = 0; j < kMaxPeers; ++j)
+                if (j < p.num_peers) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_out[j]) + off) = val;
+            }
+          }
+          __syncwarp();  // the next chunk reuses the staging area
+          continue;
+        }
+      }
+      if (!row_ok) continue;
+      const int64_t off = (orow - static_cast<uint8_t*>(p.out)) + static_cast<int64_t>(col0) * esz;
+      store_row32(static_cast<uint8_t*>(p.out) + off, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
+#pragma unroll
+      for (int j = 0; j < kMaxPeers; ++j)
+        if (j < p.num_peers)
+          store_row32(static_cast<uint8_t*>(p.peer_out[j]) + off, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
     }
   } else if (EPI == EPI_MOE) {
     const int route = p.sorted_ids[pos];
@@ -293,11 +347,12 @@ __device__ __forceinline__ void pair_epilogue_tile(const PairParams& p, const Pa
   }
 }
 
-template <int AMODE, int BMODE, int EPI, bool FP16, int DECODE_WARPS>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECODE_WARPS>::kThreads, 1)
+template <int AMODE, int BMODE, int EPI, bool FP16, int DECODE_WARPS, bool PEERS = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECODE_WARPS, PEERS>::kThreads, 1)
     mxfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const PairParams p) {
-  using Cfg = Pair2Cfg<BMODE, DECODE_WARPS>;
+  static_assert(!PEERS || EPI == EPI_DENSE, "peer stores are a dense-epilogue feature");
+  using Cfg = Pair2Cfg<BMODE, DECODE_WARPS, PEERS>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -478,7 +533,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
       if (!mbar_wait_cluster(&tfull[acc], (tl >> 1) & 1, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
-      pair_epilogue_tile<EPI>(p, c, tbase, rank, r_local, grp, esz);
+      pair_epilogue_tile<EPI, PEERS>(p, c, tbase, rank, r_local, grp, esz,
+                                     smem_u32(smem + Cfg::kOffOut) + (grp * 4 + q) * 2048);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);

@@ -117,6 +117,16 @@ _SIGNATURES = {
         [_VP, _INT, _VP, _VP, _VP, _VP, _VP, _VP, _INT, _VP, _INT, _VP, _INT, _I64, _INT, _INT, _I64, _I64,
          _INT, _VP],
     ),
+    "mxfp4_linear_w4a16_allgather": (
+        _INT,
+        [_VP, _INT, _I64, _VP, _I64, _VP, _I64, _VP, _VP, ctypes.POINTER(ctypes.c_void_p), _INT, _I64, _I64,
+         _I64, _I64, _INT, _VP, _SZ, _VP],
+    ),
+    "mxfp4_peer_barrier": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT, _INT, _VP, _VP]),
+    "mxfp4_ipc_alloc": (_INT, [_SZ, ctypes.POINTER(ctypes.c_void_p), _VP]),
+    "mxfp4_ipc_open": (_INT, [_VP, ctypes.POINTER(ctypes.c_void_p)]),
+    "mxfp4_ipc_close": (_INT, [_VP]),
+    "mxfp4_ipc_free": (_INT, [_VP]),
     "mxfp4_moe_layer_workspace_size": (_SZ, [_I64, _INT, _INT, _I64, _I64]),
     "mxfp4_moe_layer": (
         _INT,

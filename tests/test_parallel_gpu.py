@@ -44,6 +44,16 @@ def _worker(rank, world, port, q):
         # the shard GEMMs see different N, so tiles differ; each output is one
         # FP32 reduction of the same products in K order
         lin_ok = bool(torch.equal(y_tp.view(torch.int16), y_one.view(torch.int16)))
+        # the same with the all-gather fused into the GEMM epilogue (peer stores over NVLink),
+        # on the pair kernel (M=300), the few-token kernel + push (M=100) and decode-once (M=2048)
+        fused_ok = True
+        layer_f = cp.ColumnParallelLinear.from_full(w, s, rank, world, fused=True)
+        for mm in (300, 100, 2048, 300):
+            xm = torch.randn(mm, k, generator=g, device=dev).to(torch.bfloat16)
+            yf = layer_f(xm).clone()
+            ys = soft.linear_mxfp4_soft(xm, w, s)
+            fused_ok = fused_ok and bool(torch.equal(yf.view(torch.int16), ys.view(torch.int16)))
+        lin_ok = lin_ok and fused_ok
         # expert-parallel MoE: every rank owns its tokens and E/world experts
         t_local, h, e, top_k, inter = 512, 1024, 32, 4, 256
         x_all = torch.randn(world * t_local, h, generator=g, device=dev).to(torch.bfloat16)
