@@ -502,12 +502,12 @@ def _max_over_ranks(v, device):
     return t.item()
 
 
-def bench_ep_moe(soft, ep_mod, world, rank, device, steps, warmup, barrier):
+def bench_ep_moe(soft, ep_mod, world, rank, device, steps, warmup, barrier, fused=True):
     """Expert-parallel config-2 layer: T tokens in total, T/G per rank, E/G experts per rank."""
     t_local = MOE["t"] // world
     x, w13, s13, w2, s2, tw, tid = make_moe_inputs(device, seed=7, **MOE)
     sl = slice(rank * t_local, (rank + 1) * t_local)
-    layer = ep_mod.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world)
+    layer = ep_mod.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, fused=fused)
     xs, tws, tids = x[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous()
     del w13, s13, w2, s2, x, tw, tid
     for _ in range(warmup):
@@ -601,6 +601,7 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
     # expert-parallel MoE layer (config 2, tokens data-parallel across ranks)
     ep_steps = max(5, min(20, args.steps // 10))
     ms_ep, ep_nv_bytes, fm = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup, barrier)
+    ms_ep_nccl, _, _ = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup, barrier, fused=False)
     t_ep_roof = max(fm / world / (pk["bf16_tflops"] * 1e12), ep_nv_bytes / (NVLINK_GBS * 1e9))
     status = soft.device_status()
     status = int(_max_over_ranks(float(status), device))
@@ -634,7 +635,10 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
                 "experts_per_gpu": MOE["e"] // world, "tokens_per_gpu": MOE["t"] // world,
                 "roofline_target_ms": t_ep_roof * 1e3, "roofline_frac": t_ep_roof * 1e3 / ms_ep,
                 "nvlink_bytes_in_per_gpu": ep_nv_bytes,
-                "timing": "CUDA events around eager calls (host syncs on the per-destination counts), max over ranks"}},
+                "dispatch_combine": "native: peer-mapped routed buffers over NVLink, device barriers",
+                "timing": "CUDA events around eager calls, max over ranks"},
+                "config2_moe_layer_ep_nccl": {"ms": ms_ep_nccl, "tokens_per_s": MOE["t"] / (ms_ep_nccl * 1e-3),
+                                              "what": "NCCL all-to-all dispatch/combine (host syncs on counts)"}},
         }
         if status:
             line["device_status"] = status

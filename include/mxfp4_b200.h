@@ -230,6 +230,33 @@ int mxfp4_ipc_free(void* ptr);
 /* 2 s records MXFP4_ERR_TIMEOUT in the device status word and returns.     */
 int mxfp4_peer_barrier(int32_t* const* flags, int rank, int world, int32_t* counter, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Expert-parallel MoE layer.  No counterpart in the reference;  */
+/* replaces the NCCL all-to-all dispatch / local layer / all-to-all combine  */
+/* of an expert-parallel _moe_apply (vllm:233-265).  Rank `rank` of `world`  */
+/* (one process per GPU, one node) holds experts [rank*E/world, ...) as      */
+/* w13[E/world, 2*inter, hidden/2] (+ scales) and w2[E/world, hidden,        */
+/* inter/2] (+ scales), and its own num_tokens tokens with their global      */
+/* topk_ids; `out` receives the same [num_tokens, hidden] rows the           */
+/* single-GPU mxfp4_moe_layer gives for them, bit for bit.                   */
+/* Peer tables (host arrays of `world` device pointers, entry j = rank j's   */
+/* buffer mapped into this process, e.g. with mxfp4_ipc_open): counts       */
+/* [world * E] int32; xr [recv_capacity, hidden] BF16; wr [recv_capacity]   */
+/* F32; yr [recv_capacity, hidden] BF16; flags/counter as for               */
+/* mxfp4_peer_barrier.  recv_capacity = mxfp4_ep_moe_recv_capacity() of the */
+/* largest num_tokens of any rank.  Every rank calls it together (three    */
+/* device barriers inside); no host synchronisation.                        */
+int64_t mxfp4_ep_moe_recv_capacity(int64_t max_tokens_per_rank, int top_k, int num_experts, int world);
+size_t mxfp4_ep_moe_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t inter,
+                                   int64_t recv_capacity);
+int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, const void* w2,
+                       const void* w2_scale, const void* topk_weights, int w_dtype,
+                       const void* topk_ids, int ids_dtype, void* out, int64_t num_tokens,
+                       int top_k, int num_experts, int64_t hidden, int64_t inter, int rank, int world,
+                       void* const* counts, void* const* xr, void* const* wr, void* const* yr,
+                       int64_t recv_capacity, int32_t* const* flags, int32_t* counter,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,6 +7,7 @@
 #include <string>
 
 #include "elementwise.cuh"
+#include "ep.cuh"
 #include "gemm.cuh"
 #include "gemm2.cuh"
 #include "gemm_small.cuh"
@@ -1116,6 +1117,189 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   combine_topk_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(ybuf),
                                            static_cast<__nv_bfloat16*>(out), num_tokens, top_k, hidden);
   MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+
+// ---------------------------------------------------------------------------
+// Expert-parallel MoE layer (csrc/ep.cuh).
+// ---------------------------------------------------------------------------
+int64_t mxfp4_ep_moe_recv_capacity(int64_t max_tokens_per_rank, int top_k, int num_experts, int world) {
+  if (max_tokens_per_rank < 0 || top_k <= 0 || num_experts <= 0 || world <= 0 || num_experts % world) return 0;
+  const int64_t el = num_experts / world;
+  const int64_t rows = static_cast<int64_t>(world) * max_tokens_per_rank * top_k + el * (kEpBlock - 1);
+  return (rows + kEpBlock - 1) / kEpBlock * kEpBlock;
+}
+
+size_t mxfp4_ep_moe_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t inter,
+                                   int64_t recv_capacity) {
+  const int64_t routes = num_tokens * top_k;
+  size_t b = 0;
+  b += align_up(sizeof(int32_t) * num_experts, 256) * 2;                  // send_base, lstart
+  b += align_up(sizeof(int32_t) * (recv_capacity / kEpBlock + 1), 256);   // owner block experts
+  b += 256;                                                               // owner used rows
+  b += align_up(sizeof(int32_t) * std::max<int64_t>(recv_capacity, 1), 256);  // owner row ids
+  b += align_up(sizeof(int32_t) * std::max<int64_t>(routes, 1), 256) * 3; // sorted, expert per position, dst
+  b += 256;                                                               // valid routes
+  b += route_ws_bytes(routes, num_experts);
+  b += align_up(static_cast<size_t>(recv_capacity) * inter * 2, 256);     // h
+  return b;
+}
+
+int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, const void* w2, const void* w2_scale,
+                       const void* topk_weights, int w_dtype, const void* topk_ids, int ids_dtype, void* out,
+                       int64_t num_tokens, int top_k, int num_experts, int64_t hidden, int64_t inter, int rank,
+                       int world, void* const* counts, void* const* xr, void* const* wr, void* const* yr,
+                       int64_t recv_capacity, int32_t* const* flags, int32_t* counter, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(x && w13 && w13_scale && w2 && w2_scale && topk_weights && topk_ids && out, "null pointer");
+  MX_CHECK(counts && xr && wr && yr && flags && counter, "null peer table");
+  MX_CHECK(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world, "bad rank/world");
+  MX_CHECK(num_experts > 0 && num_experts <= kMaxExperts && num_experts % world == 0,
+           "num_experts must be in [1, 1024] and divide over the ranks");
+  MX_CHECK(hidden > 0 && hidden % 128 == 0 && inter > 0 && inter % 128 == 0, "hidden/inter must be multiples of 128");
+  MX_CHECK(num_tokens >= 0 && top_k > 0, "bad num_tokens/top_k");
+  MX_CHECK(w_dtype == MXFP4_DTYPE_F32 || w_dtype == MXFP4_DTYPE_BF16 || w_dtype == MXFP4_DTYPE_F16,
+           "topk_weights must be F32, BF16 or F16");
+  MX_CHECK(ids_dtype == MXFP4_DTYPE_I32 || ids_dtype == MXFP4_DTYPE_I64, "topk_ids must be I32 or I64");
+  MX_CHECK(aligned(x, 16) && aligned(out, 16), "x and out must be 16-byte aligned");
+  MX_CHECK(recv_capacity > 0 && recv_capacity % kEpBlock == 0 && recv_capacity < (int64_t(1) << 24),
+           "recv_capacity must be a positive multiple of 256 below 2^24");
+  const int64_t routes = num_tokens * top_k;
+  MX_CHECK(static_cast<int64_t>(world) * routes + (num_experts / world) * (kEpBlock - 1) <= recv_capacity ||
+               routes == 0,
+           "recv_capacity too small for this many routes");
+  const size_t need = mxfp4_ep_moe_workspace_size(num_tokens, top_k, num_experts, inter, recv_capacity);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(MXFP4_ERR_WORKSPACE, "EP MoE layer needs " + std::to_string(need) + " workspace bytes");
+  EpPeers pc{}, px{}, pw{}, py{};
+  PeerFlags pf{};
+  for (int j = 0; j < world; ++j) {
+    MX_CHECK(counts[j] && xr[j] && wr[j] && yr[j] && flags[j], "null peer buffer");
+    MX_CHECK(aligned(xr[j], 16) && aligned(yr[j], 16), "peer row buffers must be 16-byte aligned");
+    pc.p[j] = counts[j];
+    px.p[j] = xr[j];
+    pw.p[j] = wr[j];
+    py.p[j] = yr[j];
+    pf.f[j] = flags[j];
+  }
+  cudaStream_t s = as_stream(stream);
+  const int el = num_experts / world;
+  const int64_t cap = recv_capacity;
+  const int cap_blocks = static_cast<int>(cap / kEpBlock);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  auto take = [&](size_t bytes) {
+    uint8_t* q = ws;
+    ws += align_up(bytes, 256);
+    return q;
+  };
+  int32_t* send_base = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * num_experts));
+  int32_t* lstart = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * num_experts));
+  int32_t* block_expert = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (cap_blocks + 1)));
+  int32_t* post = reinterpret_cast<int32_t*>(take(256));
+  int32_t* rid = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * cap));
+  int32_t* sorted = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(routes, 1)));
+  int32_t* bexp = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(routes, 1)));
+  int32_t* dst = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(routes, 1)));
+  int32_t* nvalid = reinterpret_cast<int32_t*>(take(256));
+  uint8_t* route_ws = take(route_ws_bytes(routes, num_experts));
+  void* hbuf = take(static_cast<size_t>(cap) * inter * 2);
+
+  // 1. counts -> every rank; barrier
+  ep_count_kernel<<<1, 1024, 0, s>>>(topk_ids, ids_dtype, routes, num_experts, rank, world, pc);
+  MX_CUDA(cudaGetLastError());
+  peer_barrier_kernel<<<1, 32, 0, s>>>(pf, rank, world, counter);
+  MX_CUDA(cudaGetLastError());
+  // 2. plan + stable local order; dispatch rows into the owners' xr; barrier
+  ep_plan_kernel<<<1, 1024, 0, s>>>(static_cast<const int32_t*>(counts[rank]), num_experts, world, rank, send_base,
+                                    lstart, block_expert, post, rid, static_cast<int>(cap), cap_blocks);
+  MX_CUDA(cudaGetLastError());
+  if (routes > 0) {
+    if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, 1, sorted, bexp, nvalid, routes, route_ws, s))
+      return rc;
+    MX_CUDA(cudaMemsetAsync(dst, 0xFF, sizeof(int32_t) * routes, s));
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((routes + 7) / 8, int64_t(info.sms) * 16)));
+    ep_dispatch_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(x), hidden / 8, sorted, bexp, nvalid, send_base,
+                                            lstart, topk_weights, w_dtype, top_k, el, px, pw, dst);
+    MX_CUDA(cudaGetLastError());
+  }
+  peer_barrier_kernel<<<1, 32, 0, s>>>(pf, rank, world, counter);
+  MX_CUDA(cudaGetLastError());
+  // 3. owner: gate_up (fused SiLU * up) and down (route weight) over the received rows
+  {
+    CUtensorMap ta, tb;
+    if (int rc = make_map_2d(&ta, xr[rank], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hidden, cap, hidden * 2, kP2BK,
+                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = make_map_2d(&tb, w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hidden / 2,
+                             static_cast<uint64_t>(el) * 2 * inter, hidden / 2, kP2BK / 2, kP2HalfRows,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    PairParams p{};
+    p.N = static_cast<int>(2 * inter);
+    p.K = static_cast<int>(hidden);
+    p.bn = 256;
+    p.num_m_blocks = cap_blocks;
+    p.num_n_blocks = static_cast<int>((inter + p.bn / 2 - 1) / (p.bn / 2));
+    p.w_scales = static_cast<const uint8_t*>(w13_scale);
+    p.lds = hidden / 32;
+    p.w_rows_per_expert = 2 * inter;
+    p.glu_inter = static_cast<int>(inter);
+    p.sorted_ids = rid;
+    p.block_expert = block_expert;
+    p.num_post_padded = post;
+    p.num_routes = static_cast<int>(cap);
+    p.top_k = 1;
+    p.out = hbuf;
+    p.ldo = inter;
+    p.out_dtype = MXFP4_DTYPE_BF16;
+    p.vec_ok = 1;
+    if (int rc = routed_pair_gemm<A_TMA, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
+  }
+  {
+    CUtensorMap ta, tb;
+    if (int rc = make_map_2d(&ta, hbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inter, cap, inter * 2, kP2BK,
+                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = make_map_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inter / 2,
+                             static_cast<uint64_t>(el) * hidden, inter / 2, kP2BK / 2, kP2HalfRows,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    PairParams p{};
+    p.N = static_cast<int>(hidden);
+    p.K = static_cast<int>(inter);
+    p.bn = 256;
+    p.num_m_blocks = cap_blocks;
+    p.num_n_blocks = static_cast<int>((hidden + p.bn - 1) / p.bn);
+    p.w_scales = static_cast<const uint8_t*>(w2_scale);
+    p.lds = inter / 32;
+    p.w_rows_per_expert = hidden;
+    p.sorted_ids = rid;
+    p.block_expert = block_expert;
+    p.num_post_padded = post;
+    p.num_routes = static_cast<int>(cap);
+    p.top_k = 1;
+    p.out = yr[rank];
+    p.out_dtype = MXFP4_DTYPE_BF16;
+    p.topk_w = wr[rank];
+    p.w_dtype = MXFP4_DTYPE_F32;
+    p.mul_w = 1;
+    p.c_stride_t = hidden;
+    p.c_stride_j = 0;
+    p.vec_ok = 1;
+    if (int rc = routed_pair_gemm<A_TMA, EPI_MOE>(false, ta, tb, p, info.sms, s)) return rc;
+  }
+  peer_barrier_kernel<<<1, 32, 0, s>>>(pf, rank, world, counter);
+  MX_CUDA(cudaGetLastError());
+  // 4. combine: pull the token's rows back from their owners
+  if (num_tokens > 0) {
+    const int64_t total = num_tokens * (hidden / 8);
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, int64_t(info.sms) * 8)));
+    ep_combine_kernel<<<grid, 256, 0, s>>>(dst, py, static_cast<__nv_bfloat16*>(out), num_tokens, top_k, hidden);
+    MX_CUDA(cudaGetLastError());
+  }
   return MXFP4_OK;
 }
 

@@ -127,6 +127,14 @@ _SIGNATURES = {
     "mxfp4_ipc_open": (_INT, [_VP, ctypes.POINTER(ctypes.c_void_p)]),
     "mxfp4_ipc_close": (_INT, [_VP]),
     "mxfp4_ipc_free": (_INT, [_VP]),
+    "mxfp4_ep_moe_recv_capacity": (_I64, [_I64, _INT, _INT, _INT]),
+    "mxfp4_ep_moe_workspace_size": (_SZ, [_I64, _INT, _INT, _I64, _I64]),
+    "mxfp4_ep_moe_layer": (
+        _INT,
+        [_VP, _VP, _VP, _VP, _VP, _VP, _INT, _VP, _INT, _VP, _I64, _INT, _INT, _I64, _I64, _INT, _INT,
+         ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+         ctypes.POINTER(ctypes.c_void_p), _I64, ctypes.POINTER(ctypes.c_void_p), _VP, _VP, _SZ, _VP],
+    ),
     "mxfp4_moe_layer_workspace_size": (_SZ, [_I64, _INT, _INT, _I64, _I64]),
     "mxfp4_moe_layer": (
         _INT,

@@ -63,10 +63,22 @@ def _worker(rank, world, port, q):
         s2 = torch.randint(118, 131, (e, h, inter // 32), generator=g, device=dev, dtype=torch.uint8)
         tw, tid = torch.topk(torch.softmax(torch.randn(world * t_local, e, generator=g, device=dev), -1), top_k, -1)
         sl = slice(rank * t_local, (rank + 1) * t_local)
-        layer = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world)
-        y_ep = layer(x_all[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous())
         y_full = soft.moe_layer_mxfp4(x_all, w13, s13, w2, s2, tw, tid)[sl]
-        ep_ok = bool(torch.equal(y_ep.view(torch.int16), y_full.view(torch.int16)))
+        # NCCL all-to-all path
+        layer_n = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, fused=False)
+        y_n = layer_n(x_all[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous())
+        ep_ok = bool(torch.equal(y_n.view(torch.int16), y_full.view(torch.int16)))
+        # native path (peer-mapped dispatch/combine, device barriers): two calls on
+        # the same buffers, the second with new routes and fewer tokens on rank 1
+        layer = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world)
+        assert layer.fused
+        y_ep = layer(x_all[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous())
+        ep_ok = ep_ok and bool(torch.equal(y_ep.view(torch.int16), y_full.view(torch.int16)))
+        tw2, tid2 = torch.topk(torch.softmax(torch.randn(world * t_local, e, generator=g, device=dev), -1), top_k, -1)
+        y_full2 = soft.moe_layer_mxfp4(x_all, w13, s13, w2, s2, tw2, tid2)[sl]
+        n2 = t_local if rank == 0 else t_local - 100
+        y_ep2 = layer(x_all[sl][:n2].contiguous(), tw2[sl][:n2].contiguous(), tid2[sl][:n2].contiguous())
+        ep_ok = ep_ok and bool(torch.equal(y_ep2.view(torch.int16), y_full2[:n2].view(torch.int16)))
         torch.cuda.synchronize()
         q.put((rank, lin_ok, ep_ok, soft.device_status()))
     finally:
