@@ -1115,7 +1115,8 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   const int64_t vecs = num_tokens * (hidden / 8);
   const int grid = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, int64_t(info.sms) * 8));
   combine_topk_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(ybuf),
-                                           static_cast<__nv_bfloat16*>(out), num_tokens, top_k, hidden);
+                                           static_cast<__nv_bfloat16*>(out), num_tokens, top_k, hidden, topk_ids,
+                                           ids_dtype, num_experts);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
 }

@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
 __global__ void __launch_bounds__(256) combine_topk_kernel(const __nv_bfloat16* __restrict__ rows,
                                                            __nv_bfloat16* __restrict__ out,
                                                            int64_t num_tokens, int top_k,
-                                                           int64_t hidden) {
+                                                           int64_t hidden, const void* __restrict__ ids,
+                                                           int ids_dtype, int num_experts) {
   const int64_t vec_per_row = hidden / 8;
   const int64_t total = num_tokens * vec_per_row;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -277,6 +278,10 @@ __global__ void __launch_bounds__(256) combine_topk_kernel(const __nv_bfloat16* 
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
     for (int j = 0; j < top_k; ++j) {
+      // a route to an expert outside [0, E) was not computed and contributes
+      // zero, as its all-zero rows do in the reference composition
+      const int e = load_expert(ids, ids_dtype, t * top_k + j);
+      if (e < 0 || e >= num_experts) continue;
       const uint4 q = *reinterpret_cast<const uint4*>(rows + ((t * top_k + j) * hidden) + v * 8);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll

@@ -141,6 +141,25 @@ def test_moe_layer_matches_oracle(t, h, e, k, inter):
     assert torch.equal(two_op.view(torch.int16), y.view(torch.int16))
 
 
+def test_moe_layer_out_of_range_ids_contribute_zero():
+    t, h, e, k, inter = 70, 256, 6, 3, 128
+    g = torch.Generator().manual_seed(77)
+    x = torch.randn(t, h, generator=g).to(torch.bfloat16)
+    w13 = torch.randint(0, 256, (e, 2 * inter, h // 2), generator=g, dtype=torch.uint8)
+    s13 = torch.randint(118, 131, (e, 2 * inter, h // 32), generator=g, dtype=torch.uint8)
+    w2 = torch.randint(0, 256, (e, h, inter // 2), generator=g, dtype=torch.uint8)
+    s2 = torch.randint(114, 127, (e, h, inter // 32), generator=g, dtype=torch.uint8)
+    tw = torch.rand(t, k, generator=g)
+    tid = torch.randint(0, e, (t, k), generator=g)
+    tid[::3, 1] = e          # past the last expert: dropped
+    tid[5, :] = e + 7        # a token with every route dropped
+    y = soft.moe_layer_mxfp4(x.cuda(), w13.cuda(), s13.cuda(), w2.cuda(), s2.cuda(), tw.cuda(), tid.cuda())
+    ref = O.moe_layer(_np(x), w13.numpy(), s13.numpy(), w2.numpy(), s2.numpy(), tw.numpy(), tid.numpy())
+    ok, err, bound, rel = O.check_close(_np(y), ref)
+    assert ok, (err, bound, rel)
+    assert torch.count_nonzero(y[5]).item() == 0
+
+
 def test_moe_layer_config2_full_size():
     # BASELINE config 2 (Qwen3-30B-A3B layer): T=4096, H=2048, E=128, k=8, I=768
     t, h, e, k, inter = 4096, 2048, 128, 8, 768
