@@ -31,24 +31,27 @@ constexpr int kP2ABytes = kP2HalfRows * kP2BK * 2;    // 16 KB
 constexpr int kP2BBytes = kP2HalfRows * kP2BK * 2;    // 16 KB
 constexpr int kP2PBytes = kP2HalfRows * kP2BK / 2;    // 4 KB
 
-// PEERS: the dense epilogue also stores into other ranks' buffers; it stages
-// each warp's 32 x 32 output chunk in shared memory (2 KB per epilogue warp)
-// so that every global store of the warp covers whole 64-byte row segments,
-// the unit that crosses NVLink efficiently.
+// PEERS (dense all-gather): the epilogue stages each warp's 32 x 32 output
+// chunk in shared memory (2 KB per epilogue warp) and stores whole 64-byte row
+// segments locally, releases the accumulator, and hands the finished tile to
+// four pusher warps, which copy its rows from the local output into every
+// peer's buffer while the tensor cores work on the next tile.
 template <int BMODE, int DECODE_WARPS, bool PEERS = false>
 struct Pair2Cfg {
   static constexpr int kStages = (BMODE == B_DECODE && PEERS) ? 5 : 6;
   static constexpr int kDecodeWarps = BMODE == B_DECODE ? DECODE_WARPS : 0;
-  // warps 0-3 control, 4-7 epilogue group 0, then the decoders, then epilogue group 1
+  // warps 0-3 control, 4-7 epilogue group 0, then the decoders, then epilogue
+  // group 1, then (PEERS) the pushers
   static constexpr int kEpi1Warp = 8 + kDecodeWarps;
-  static constexpr int kThreads = 256 + 32 * kDecodeWarps + 128;
+  static constexpr int kPushWarp = kEpi1Warp + 4;
+  static constexpr int kThreads = 256 + 32 * kDecodeWarps + 128 + (PEERS ? 128 : 0);
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kP2ABytes;
   static constexpr int kOffP = kOffB + kStages * kP2BBytes;
   static constexpr int kOffOut = kOffP + (BMODE == B_DECODE ? kStages * kP2PBytes : 0);
   static constexpr int kOffBar = kOffOut + (PEERS ? 8 * 2048 : 0);
-  // full, ready, empty per stage; tfull[2], tempty[2], drain
-  static constexpr int kNumBars = 3 * kStages + 5;
+  // full, ready, empty per stage; tfull[2], tempty[2], drain; (PEERS) stored[2], pushed[2]
+  static constexpr int kNumBars = 3 * kStages + 5 + (PEERS ? 4 : 0);
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
 };
@@ -277,9 +280,6 @@ __device__ __forceinline__ void pair_epilogue_tile(const PairParams& p, const Pa
             if (row0 + rr < p.M) {
               const int64_t off = (static_cast<int64_t>(row0 + rr) * p.ldo + col0 + ch * 8) * 2;
               *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + off) = val;
-#pragma unroll
-              for (int j = 0; j < kMaxPeers; ++j)
-                if (j < p.num_peers) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_out[j]) + off) = val;
             }
           }
           __syncwarp();  // the next chunk reuses the staging area
@@ -287,12 +287,7 @@ __device__ __forceinline__ void pair_epilogue_tile(const PairParams& p, const Pa
         }
       }
       if (!row_ok) continue;
-      const int64_t off = (orow - static_cast<uint8_t*>(p.out)) + static_cast<int64_t>(col0) * esz;
-      store_row32(static_cast<uint8_t*>(p.out) + off, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
-#pragma unroll
-      for (int j = 0; j < kMaxPeers; ++j)
-        if (j < p.num_peers)
-          store_row32(static_cast<uint8_t*>(p.peer_out[j]) + off, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
+      store_row32(orow + static_cast<int64_t>(col0) * esz, p.out_dtype, v, p.N - col0, p.vec_ok != 0);
     }
   } else if (EPI == EPI_MOE) {
     const int route = p.sorted_ids[pos];
@@ -347,6 +342,55 @@ __device__ __forceinline__ void pair_epilogue_tile(const PairParams& p, const Pa
   }
 }
 
+// Pushers (PEERS): copy this CTA's rows [row0, row0 + 128) x columns
+// [col0, col0 + width) of the finished tile from the local output (L2-hot,
+// read past L1) into every peer buffer at the same offset; 128 threads, 16-byte
+// vectors when the rows allow, four loads in flight per thread.
+__device__ __forceinline__ void push_tile_rows(const PairParams& p, int row0, int col0, int width, int esz,
+                                               int tid) {
+  const int rows = p.M - row0 < 128 ? p.M - row0 : 128;
+  if (rows <= 0 || width <= 0) return;
+  const int64_t row_bytes = static_cast<int64_t>(width) * esz;
+  const int64_t ld_bytes = p.ldo * esz;
+  const uint8_t* src = static_cast<const uint8_t*>(p.out) + static_cast<int64_t>(row0) * ld_bytes +
+                       static_cast<int64_t>(col0) * esz;
+  const int64_t off0 = src - static_cast<const uint8_t*>(p.out);
+  if (p.vec_ok && row_bytes % 16 == 0) {
+    const int per_row = static_cast<int>(row_bytes / 16);
+    const int total = rows * per_row;
+    for (int base = tid; base < total; base += 4 * 128) {
+      uint4 v[4];
+      int64_t off[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * 128;
+        off[u] = -1;
+        if (i < total) {
+          off[u] = static_cast<int64_t>(i / per_row) * ld_bytes + static_cast<int64_t>(i % per_row) * 16;
+          v[u] = __ldcg(reinterpret_cast<const uint4*>(src + off[u]));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (off[u] >= 0) {
+#pragma unroll
+          for (int j = 0; j < kMaxPeers; ++j)
+            if (j < p.num_peers) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_out[j]) + off0 + off[u]) = v[u];
+        }
+    }
+  } else {
+    const int per_row = static_cast<int>(row_bytes / 2);
+    const int total = rows * per_row;
+    for (int i = tid; i < total; i += 128) {
+      const int64_t off = static_cast<int64_t>(i / per_row) * ld_bytes + static_cast<int64_t>(i % per_row) * 2;
+      const uint16_t v = __ldcg(reinterpret_cast<const unsigned short*>(src + off));
+#pragma unroll
+      for (int j = 0; j < kMaxPeers; ++j)
+        if (j < p.num_peers) *reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(p.peer_out[j]) + off0 + off) = v;
+    }
+  }
+}
+
 template <int AMODE, int BMODE, int EPI, bool FP16, int DECODE_WARPS, bool PEERS = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECODE_WARPS, PEERS>::kThreads, 1)
     mxfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -363,6 +407,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
   uint64_t* tfull = bars + 3 * S;
   uint64_t* tempty = bars + 3 * S + 2;
   uint64_t* drain = bars + 3 * S + 4;
+  uint64_t* stored = bars + 3 * S + 5;  // PEERS only
+  uint64_t* pushed = stored + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
 
@@ -385,6 +431,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
       mbar_init(&tempty[a], 16);  // 2 epilogue groups x 4 warps x 2 CTAs
     }
     mbar_init(drain, 1);
+    if constexpr (PEERS) {
+      for (int a = 0; a < 2; ++a) {
+        mbar_init(&stored[a], 8);  // the 8 epilogue warps of this CTA
+        mbar_init(&pushed[a], 4);  // the 4 pusher warps
+      }
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -538,6 +590,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+      if constexpr (PEERS) {
+        // the tile's local rows are stored: hand them to the pushers (which must
+        // be done with the tile two back, the last user of this barrier slot)
+        if (!mbar_wait(&pushed[acc], ((tl >> 1) & 1) ^ 1, abort_flag)) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&stored[acc]);
+      }
+    }
+  } else if (PEERS && warp >= Cfg::kPushWarp && warp < Cfg::kPushWarp + 4) {
+    // ------------------------------------------------------------------ pushers (PEERS, both CTAs)
+    if constexpr (PEERS) {
+      const int tid = threadIdx.x - Cfg::kPushWarp * 32;
+      const int esz = out_esize(p.out_dtype);
+      int tl = 0;
+      for (int t = cluster_id; t < num_tiles; t += num_clusters, ++tl) {
+        const PairTile c = pair_tile<EPI>(p, t, nmb);
+        const int acc = tl & 1;
+        if (!mbar_wait(&stored[acc], (tl >> 1) & 1, abort_flag)) break;
+        const int row0 = c.m_blk * kP2BM + static_cast<int>(rank) * kP2HalfRows;
+        const int col0 = c.n_blk * p.bn;
+        const int width = p.N - col0 < p.bn ? p.N - col0 : p.bn;
+        push_tile_rows(p, row0, col0, width, esz, tid);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pushed[acc]);
+      }
     }
   } else if (warp >= 8 && warp < Cfg::kEpi1Warp) {
     // ------------------------------------------------------------------ decoders (both CTAs)
