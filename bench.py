@@ -558,6 +558,8 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
     ms_nccl = _max_over_ranks(time_graphs(gs, args.steps, args.warmup, barrier=barrier), device)
     del gs, nccl_sets
     gs = graphs_for(lambda x, layer: layer(x), sets, torch.cuda.Stream())
+    ag_path = ("NVSwitch multicast stores" if getattr(sets[0][1]._bufs[0], "multicast_ptr", 0)
+               else "peer stores over NVLink")
     sampler = ClockSampler(device.index)
     ms = _max_over_ranks(time_graphs(gs, args.steps, args.warmup, barrier=barrier, sampler=sampler), device)
     del gs
@@ -613,7 +615,7 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE config-1 distributions, seeded)",
             "config": {"workload": "config1_qkv_prefill", "M": m, "N": n, "K": k, "backend": "fused",
                        "parallelism": f"tp{world}: column-sharded W (N/{world} rows per GPU), all-gather fused "
-                                      "into the GEMM epilogue (peer stores over NVLink) + device barrier",
+                                      f"into the GEMM epilogue ({ag_path}) + device barrier",
                        "l2": "4 rotating input sets of 64 MB (working set > 126 MB L2)",
                        "timing": "CUDA graph of the 4-set rotation replayed, CUDA events, max over ranks"},
             "roofline": {"bound": "tensor", "achieved": gemm_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",

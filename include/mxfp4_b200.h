@@ -193,8 +193,8 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
                     size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
-/* Multi-GPU dense linear (column-sharded).  No counterpart in    */
-/* the reference; replaces the shard GEMM + NCCL all-gather pair.           */
+/* Multi-GPU dense linear (column-sharded).  No counterpart in the          */
+/* reference; replaces the shard GEMM + NCCL all-gather pair.               */
 /* mxfp4_linear_w4a16 whose output block is also written, from the GEMM     */
 /* epilogue, into the buffers of up to 7 other ranks on this node: `out` is */
 /* this rank's [m, n] column block inside its full [m, n * world] output    */
@@ -208,6 +208,19 @@ int mxfp4_linear_w4a16_allgather(const void* x, int x_dtype, int64_t ldx, const 
                                  void* out, void* const* peer_out, int num_peers, int64_t ldo,
                                  int64_t m, int64_t n, int64_t k, int mode, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* The same with an NVLink multicast mapping of all ranks' outputs (NVSwitch */
+/* multicast object, e.g. the multicast address of a torch symmetric-memory */
+/* buffer), offset to this rank's block like peer_out.  Each 16-byte chunk  */
+/* is stored once through out_mc and NVSwitch writes it into every rank's   */
+/* buffer, so this GPU sends its block once instead of once per peer;       */
+/* peer_out (num_peers >= 1) is still used for rows whose width or stride   */
+/* is not a multiple of 16 bytes.  No counterpart in the reference.         */
+int mxfp4_linear_w4a16_allgather_mc(const void* x, int x_dtype, int64_t ldx, const void* w_packed,
+                                    int64_t ldw, const void* w_scales, int64_t lds, const void* bias,
+                                    void* out, void* const* peer_out, int num_peers, void* out_mc,
+                                    int64_t ldo, int64_t m, int64_t n, int64_t k, int mode,
+                                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* Peer-mapped buffers for the multi-GPU paths (CUDA IPC; one process per   */
 /* GPU on one node).  mxfp4_ipc_alloc: zero-filled device allocation of the  */
@@ -231,7 +244,7 @@ int mxfp4_ipc_free(void* ptr);
 int mxfp4_peer_barrier(int32_t* const* flags, int rank, int world, int32_t* counter, void* stream);
 
 /* ------------------------------------------------------------------------ */
-/* Expert-parallel MoE layer.  No counterpart in the reference;  */
+/* Expert-parallel MoE layer.  No counterpart in the reference;             */
 /* replaces the NCCL all-to-all dispatch / local layer / all-to-all combine  */
 /* of an expert-parallel _moe_apply (vllm:233-265).  Rank `rank` of `world`  */
 /* (one process per GPU, one node) holds experts [rank*E/world, ...) as      */

@@ -129,6 +129,7 @@ int elem_size(int dtype) {
 struct PeerOut {
   int n = 0;
   void* p[kMaxPeers] = {};
+  void* mc = nullptr;  // multicast mapping of all ranks' outputs (16-byte stores), or null
 };
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -418,9 +419,13 @@ __global__ void __launch_bounds__(256) push_rows_kernel(const uint8_t* __restric
     const int64_t off = r * ld_bytes + u * (vec ? 16 : 2);
     if (vec) {
       const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+      if (peers.mc != nullptr) {
+        multimem_st_v4(static_cast<uint8_t*>(peers.mc) + off, v);
+      } else {
 #pragma unroll
-      for (int j = 0; j < kMaxPeers; ++j)
-        if (j < peers.n) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.p[j]) + off) = v;
+        for (int j = 0; j < kMaxPeers; ++j)
+          if (j < peers.n) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.p[j]) + off) = v;
+      }
     } else {
       const uint16_t v = *reinterpret_cast<const uint16_t*>(src + off);
 #pragma unroll
@@ -564,6 +569,7 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
   p.vec_ok = aligned(out, 16) && (ldo * 2) % 16 == 0;
   p.num_peers = peers.n;
   for (int j = 0; j < kMaxPeers; ++j) p.peer_out[j] = j < peers.n ? peers.p[j] : nullptr;
+  p.mc_out = peers.mc;
   if (peers.n > 0) {
     bool peers_aligned = true;
     for (int j = 0; j < peers.n; ++j) peers_aligned = peers_aligned && aligned(peers.p[j], 16);
@@ -657,6 +663,25 @@ int mxfp4_linear_w4a16_allgather(const void* x, int x_dtype, int64_t ldx, const 
   MX_CHECK(num_peers == 0 || peer_out != nullptr, "null peer_out");
   PeerOut peers{};
   peers.n = num_peers;
+  for (int j = 0; j < num_peers; ++j) {
+    MX_CHECK(peer_out[j] != nullptr, "null peer output pointer");
+    peers.p[j] = peer_out[j];
+  }
+  return linear_impl(x, x_dtype, ldx, w_packed, ldw, w_scales, lds, bias, out, ldo, m, n, k, mode, workspace,
+                     workspace_bytes, stream, peers);
+}
+
+int mxfp4_linear_w4a16_allgather_mc(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw,
+                                    const void* w_scales, int64_t lds, const void* bias, void* out,
+                                    void* const* peer_out, int num_peers, void* out_mc, int64_t ldo, int64_t m,
+                                    int64_t n, int64_t k, int mode, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  MX_CHECK(num_peers >= 1 && num_peers <= kMaxPeers, "num_peers must be in [1, 7]");
+  MX_CHECK(peer_out != nullptr && out_mc != nullptr, "null peer_out or out_mc");
+  MX_CHECK(reinterpret_cast<uintptr_t>(out_mc) % 16 == 0, "out_mc must be 16-byte aligned");
+  PeerOut peers{};
+  peers.n = num_peers;
+  peers.mc = out_mc;
   for (int j = 0; j < num_peers; ++j) {
     MX_CHECK(peer_out[j] != nullptr, "null peer output pointer");
     peers.p[j] = peer_out[j];

@@ -169,6 +169,9 @@ struct PairParams {
   // columns; ldo is the full row stride)
   int num_peers;
   void* peer_out[kMaxPeers];
+  // optional NVLink multicast mapping of all ranks' outputs, offset like
+  // peer_out: one multimem store reaches every rank (16-byte path only)
+  void* mc_out;
 };
 using DenseParams = PairParams;
 
@@ -346,6 +349,14 @@ __device__ __forceinline__ void pair_epilogue_tile(const PairParams& p, const Pa
 // [col0, col0 + width) of the finished tile from the local output (L2-hot,
 // read past L1) into every peer buffer at the same offset; 128 threads, 16-byte
 // vectors when the rows allow, four loads in flight per thread.
+// One 16-byte store to a multicast address: NVSwitch writes it into every
+// rank's buffer bound to the multicast object.
+__device__ __forceinline__ void multimem_st_v4(void* mc_addr, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)), "f"(__uint_as_float(v.w))
+               : "memory");
+}
+
 __device__ __forceinline__ void push_tile_rows(const PairParams& p, int row0, int col0, int width, int esz,
                                                int tid) {
   const int rows = p.M - row0 < 128 ? p.M - row0 : 128;
@@ -373,9 +384,13 @@ __device__ __forceinline__ void push_tile_rows(const PairParams& p, int row0, in
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         if (off[u] >= 0) {
+          if (p.mc_out != nullptr) {
+            multimem_st_v4(static_cast<uint8_t*>(p.mc_out) + off0 + off[u], v[u]);
+          } else {
 #pragma unroll
-          for (int j = 0; j < kMaxPeers; ++j)
-            if (j < p.num_peers) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_out[j]) + off0 + off[u]) = v[u];
+            for (int j = 0; j < kMaxPeers; ++j)
+              if (j < p.num_peers) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.peer_out[j]) + off0 + off[u]) = v[u];
+          }
         }
     }
   } else {

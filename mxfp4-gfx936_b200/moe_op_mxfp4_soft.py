@@ -122,6 +122,11 @@ _SIGNATURES = {
         [_VP, _INT, _I64, _VP, _I64, _VP, _I64, _VP, _VP, ctypes.POINTER(ctypes.c_void_p), _INT, _I64, _I64,
          _I64, _I64, _INT, _VP, _SZ, _VP],
     ),
+    "mxfp4_linear_w4a16_allgather_mc": (
+        _INT,
+        [_VP, _INT, _I64, _VP, _I64, _VP, _I64, _VP, _VP, ctypes.POINTER(ctypes.c_void_p), _INT, _VP, _I64, _I64,
+         _I64, _I64, _INT, _VP, _SZ, _VP],
+    ),
     "mxfp4_peer_barrier": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT, _INT, _VP, _VP]),
     "mxfp4_ipc_alloc": (_INT, [_SZ, ctypes.POINTER(ctypes.c_void_p), _VP]),
     "mxfp4_ipc_open": (_INT, [_VP, ctypes.POINTER(ctypes.c_void_p)]),

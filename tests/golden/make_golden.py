@@ -1,9 +1,9 @@
 """Generate the golden fixtures under tests/golden/ from the reference's own code.
 
-Run in a container that has the reference checkout (default location
-``/root/reference``, override with ``MXFP4_REFERENCE_ROOT``)::
+Run in a container that has the reference checkout, with
+``MXFP4_REFERENCE_ROOT`` set to its root directory::
 
-    python tests/golden/make_golden.py
+    MXFP4_REFERENCE_ROOT=/path/to/reference python tests/golden/make_golden.py
 
 The GPU box never runs this script; it only reads the ``.npz`` files it
 writes.  What comes from where (paths relative to the reference root):
@@ -39,7 +39,7 @@ import torch
 import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.getenv("MXFP4_REFERENCE_ROOT", "/root/reference"))
+REF = Path(os.getenv("MXFP4_REFERENCE_ROOT", ""))
 
 
 def _load_by_path(name: str, path: Path):
@@ -81,6 +81,8 @@ def as_bits(t: torch.Tensor) -> np.ndarray:
 
 
 def main() -> None:
+    if not os.getenv("MXFP4_REFERENCE_ROOT"):
+        raise SystemExit("set MXFP4_REFERENCE_ROOT to the reference checkout's root directory")
     soft, ref_test, vf = load_reference()
     os.environ["MXFP4_GFX936_BACKEND"] = "safe"
     quant = ref_test.torch_dynamic_mxfp4_quant

@@ -1,6 +1,6 @@
 """Multi-GPU paths on real GPUs (NCCL over NVLink): the column-sharded linear
 and the expert-parallel MoE layer must reproduce the single-GPU results bit
-for bit.  Skipped on machines with fewer than two GPUs."""
+for bit.  Each world size is skipped on machines with fewer GPUs."""
 
 import os
 import socket
@@ -46,13 +46,19 @@ def _worker(rank, world, port, q):
         lin_ok = bool(torch.equal(y_tp.view(torch.int16), y_one.view(torch.int16)))
         # the same with the all-gather fused into the GEMM epilogue (peer stores over NVLink),
         # on the pair kernel (M=300), the few-token kernel + push (M=100) and decode-once (M=2048)
+        # -- with per-peer stores into CUDA IPC mappings, and with NVSwitch multicast
+        # stores where the GPUs support them
+        from torch._C._distributed_c10d import _SymmetricMemory
+        from torch.distributed._symmetric_memory import DeviceType
+        modes = [False] + ([True] if _SymmetricMemory.has_multicast_support(DeviceType.CUDA, rank) else [])
         fused_ok = True
-        layer_f = cp.ColumnParallelLinear.from_full(w, s, rank, world, fused=True)
-        for mm in (300, 100, 2048, 300):
-            xm = torch.randn(mm, k, generator=g, device=dev).to(torch.bfloat16)
-            yf = layer_f(xm).clone()
-            ys = soft.linear_mxfp4_soft(xm, w, s)
-            fused_ok = fused_ok and bool(torch.equal(yf.view(torch.int16), ys.view(torch.int16)))
+        for mcast in modes:
+            layer_f = cp.ColumnParallelLinear.from_full(w, s, rank, world, fused=True, multicast=mcast)
+            for mm in (300, 100, 2048, 300):
+                xm = torch.randn(mm, k, generator=g, device=dev).to(torch.bfloat16)
+                yf = layer_f(xm).clone()
+                ys = soft.linear_mxfp4_soft(xm, w, s)
+                fused_ok = fused_ok and bool(torch.equal(yf.view(torch.int16), ys.view(torch.int16)))
         lin_ok = lin_ok and fused_ok
         # expert-parallel MoE: every rank owns its tokens and E/world experts
         t_local, h, e, top_k, inter = 512, 1024, 32, 4, 256
@@ -85,16 +91,18 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_column_parallel_and_expert_parallel_two_gpus():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_column_parallel_and_expert_parallel(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
     res = sorted(q.get(timeout=5) for _ in procs)
     assert all(p.exitcode == 0 for p in procs)
-    assert res == [(0, True, True, 0), (1, True, True, 0)], res
+    assert res == [(r, True, True, 0) for r in range(world)], res
