@@ -385,6 +385,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the non-headline configurations")
+    ap.add_argument("--decode-m", type=int, default=1, help="rows of x for --workload decode (qkv weights)")
     ap.add_argument("--workload", default=None, choices=["qkv", "oproj", "safe", "decode", "moe", "w4a4"],
                     help="run only this configuration (for profiling); prints its timing as JSON")
     args = ap.parse_args()
@@ -483,7 +484,8 @@ def run_one(args, soft, device):
     elif w == "safe":
         ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "safe", device, seed0=20)
     elif w == "decode":
-        ms = bench_linear(soft, (1, QKV[1], QKV[2]), args.steps, args.warmup, 32, "fused", device, seed0=101)
+        ms = bench_linear(soft, (args.decode_m, QKV[1], QKV[2]), args.steps, args.warmup, 32, "fused", device,
+                          seed0=101)
     elif w == "moe":
         ms = bench_moe(soft, args.steps, args.warmup, device)
     else:
