@@ -17,13 +17,16 @@ activation copy in, the output copy out, every step).
 
 At N=1 the other BASELINE configurations are measured as ``extra`` entries
 (o_proj, the decode sweep, the safe mode, the MoE layer of config 2).  With
-N>1 ranks (torchrun, NCCL) the headline is the column-sharded linear: each
-rank owns N/G output columns and an NCCL all-gather assembles the output
-(strong scaling, total work fixed); its ``roofline`` is the shard GEMM's and
+N>1 ranks (torchrun, one process per GPU) the headline is the column-sharded
+linear: each rank owns N/G output columns and the GEMM epilogue stores every
+tile into all ranks' outputs over NVLink (per-peer stores, or NVSwitch
+multicast stores from 8 GPUs on), followed by a device barrier (strong
+scaling, total work fixed); its ``roofline`` is the shard GEMM's and
 ``step_roofline`` is the slower of that GEMM at the bf16 peak and the
-all-gather bytes at the measured NVLink rate.  The expert-parallel MoE layer
-(config 2, T/G tokens and E/G experts per rank, NCCL all-to-all dispatch and
-combine) is reported as an ``extra`` entry.
+all-gather bytes at the measured NVLink rate.  The same linear with an NCCL
+all-gather, and the expert-parallel MoE layer of config 2 (T/G tokens and E/G
+experts per rank; native peer-memory dispatch and combine, and the NCCL
+all-to-all path) are ``extra`` entries.
 
 ``--impl reference`` times the reference's safe path restated with PyTorch CPU
 ops (oracle/ref_cpu.py) on this machine's host cores for the same workload; the
@@ -505,25 +508,42 @@ def _max_over_ranks(v, device):
 
 
 def bench_ep_moe(soft, ep_mod, world, rank, device, steps, warmup, barrier, fused=True):
-    """Expert-parallel config-2 layer: T tokens in total, T/G per rank, E/G experts per rank."""
+    """Expert-parallel config-2 layer: T tokens in total, T/G per rank, E/G experts per rank.
+
+    The native layer (no host synchronisation inside a call) is timed like the
+    single-GPU layer: CUDA-graph replays rotating input sets, each with its own
+    weights, enough of them that one rotation's expert weights exceed the L2.
+    The NCCL path syncs the host on the route counts, so it is timed eagerly."""
     t_local = MOE["t"] // world
-    x, w13, s13, w2, s2, tw, tid = make_moe_inputs(device, seed=7, **MOE)
     sl = slice(rank * t_local, (rank + 1) * t_local)
-    layer = ep_mod.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, fused=fused)
-    xs, tws, tids = x[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous()
-    del w13, s13, w2, s2, x, tw, tid
-    for _ in range(warmup):
-        layer(xs, tws, tids)
+    w_bytes_rank = MOE["e"] // world * 3 * MOE["inter"] * MOE["h"] * (0.5 + 1 / 32)
+    n_sets = max(2, -(-int(160e6) // int(w_bytes_rank))) if fused else 1
+    sets = []
+    for i in range(n_sets):
+        x, w13, s13, w2, s2, tw, tid = make_moe_inputs(device, seed=7 + i, **MOE)
+        layer = ep_mod.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, fused=fused)
+        sets.append((x[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous(), layer))
+        del w13, s13, w2, s2, x, tw, tid
+    if fused:
+        gs = graphs_for(lambda xs, tws, tids, layer: layer(xs, tws, tids), sets, torch.cuda.Stream())
+        ms = _max_over_ranks(time_graphs(gs, steps, warmup, barrier=barrier), device)
+        del gs
+    else:
+        xs, tws, tids, layer = sets[0]
+        for _ in range(warmup):
+            layer(xs, tws, tids)
+        torch.cuda.synchronize()
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            layer(xs, tws, tids)
+        end.record()
+        end.synchronize()
+        barrier()
+        ms = _max_over_ranks(start.elapsed_time(end) / steps, device)
     torch.cuda.synchronize()
     barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
-        layer(xs, tws, tids)
-    end.record()
-    end.synchronize()
-    barrier()
-    ms = _max_over_ranks(start.elapsed_time(end) / steps, device)
     routes_local = t_local * MOE["k"]
     # bytes a rank must receive over NVLink per step: dispatched rows from the
     # other ranks plus their combined rows coming back (uniform routing)
@@ -640,7 +660,8 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
                 "roofline_target_ms": t_ep_roof * 1e3, "roofline_frac": t_ep_roof * 1e3 / ms_ep,
                 "nvlink_bytes_in_per_gpu": ep_nv_bytes,
                 "dispatch_combine": "native: peer-mapped routed buffers over NVLink, device barriers",
-                "timing": "CUDA events around eager calls, max over ranks"},
+                "timing": "CUDA graph of rotating input sets (expert weights > L2) replayed, CUDA events, "
+                          "max over ranks"},
                 "config2_moe_layer_ep_nccl": {"ms": ms_ep_nccl, "tokens_per_s": MOE["t"] / (ms_ep_nccl * 1e-3),
                                               "what": "NCCL all-to-all dispatch/combine (host syncs on counts)"}},
         }
