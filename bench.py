@@ -524,11 +524,18 @@ def bench_ep_moe(soft, ep_mod, world, rank, device, steps, warmup, barrier, fuse
         layer = ep_mod.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, fused=fused)
         sets.append((x[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous(), layer))
         del w13, s13, w2, s2, x, tw, tid
+    ms = None
+    timing = "eager"
     if fused:
-        gs = graphs_for(lambda xs, tws, tids, layer: layer(xs, tws, tids), sets, torch.cuda.Stream())
-        ms = _max_over_ranks(time_graphs(gs, steps, warmup, barrier=barrier), device)
-        del gs
-    else:
+        try:
+            gs = graphs_for(lambda xs, tws, tids, layer: layer(xs, tws, tids), sets, torch.cuda.Stream())
+            ms = _max_over_ranks(time_graphs(gs, steps, warmup, barrier=barrier), device)
+            timing = "graph"
+            del gs
+        except RuntimeError:  # every rank takes the same path: capture fails alike everywhere
+            torch.cuda.synchronize()
+            barrier()
+    if ms is None:
         xs, tws, tids, layer = sets[0]
         for _ in range(warmup):
             layer(xs, tws, tids)
@@ -548,7 +555,7 @@ def bench_ep_moe(soft, ep_mod, world, rank, device, steps, warmup, barrier, fuse
     # bytes a rank must receive over NVLink per step: dispatched rows from the
     # other ranks plus their combined rows coming back (uniform routing)
     nv_bytes = 2 * routes_local * (world - 1) / world * MOE["h"] * 2
-    return ms, nv_bytes, moe_flops()
+    return ms, nv_bytes, moe_flops(), timing
 
 
 def run_sharded(args, soft, world, rank, device, pk, pk_kind):
@@ -624,8 +631,10 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
 
     # expert-parallel MoE layer (config 2, tokens data-parallel across ranks)
     ep_steps = max(5, min(20, args.steps // 10))
-    ms_ep, ep_nv_bytes, fm = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup, barrier)
-    ms_ep_nccl, _, _ = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup, barrier, fused=False)
+    ms_ep, ep_nv_bytes, fm, ep_timing = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup,
+                                                     barrier)
+    ms_ep_nccl, _, _, _ = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup, barrier,
+                                       fused=False)
     t_ep_roof = max(fm / world / (pk["bf16_tflops"] * 1e12), ep_nv_bytes / (NVLINK_GBS * 1e9))
     status = soft.device_status()
     status = int(_max_over_ranks(float(status), device))
@@ -660,8 +669,8 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
                 "roofline_target_ms": t_ep_roof * 1e3, "roofline_frac": t_ep_roof * 1e3 / ms_ep,
                 "nvlink_bytes_in_per_gpu": ep_nv_bytes,
                 "dispatch_combine": "native: peer-mapped routed buffers over NVLink, device barriers",
-                "timing": "CUDA graph of rotating input sets (expert weights > L2) replayed, CUDA events, "
-                          "max over ranks"},
+                "timing": ("CUDA graph of rotating input sets (expert weights > L2) replayed, CUDA events, "
+                           "max over ranks") if ep_timing == "graph" else "CUDA events around eager calls, max over ranks"},
                 "config2_moe_layer_ep_nccl": {"ms": ms_ep_nccl, "tokens_per_s": MOE["t"] / (ms_ep_nccl * 1e-3),
                                               "what": "NCCL all-to-all dispatch/combine (host syncs on counts)"}},
         }

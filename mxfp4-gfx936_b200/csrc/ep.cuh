@@ -35,9 +35,19 @@ __global__ void __launch_bounds__(1024) ep_count_kernel(const void* __restrict__
   __shared__ int hist[kMaxExperts];
   for (int e = threadIdx.x; e < num_experts; e += blockDim.x) hist[e] = 0;
   __syncthreads();
-  for (int64_t r = threadIdx.x; r < routes; r += blockDim.x) {
-    const int e = load_expert(ids, ids_dtype, r);
-    if (e >= 0 && e < num_experts) atomicAdd(&hist[e], 1);
+  // ids in batches of 8 per thread, all loads issued before the atomics: one
+  // memory latency per batch instead of one per route
+  constexpr int kBatch = 8;
+  for (int64_t base = threadIdx.x; base < routes; base += static_cast<int64_t>(blockDim.x) * kBatch) {
+    int e[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t r = base + static_cast<int64_t>(u) * blockDim.x;
+      e[u] = r < routes ? load_expert(ids, ids_dtype, r) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (e[u] >= 0 && e[u] < num_experts) atomicAdd(&hist[e[u]], 1);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < world * num_experts; i += blockDim.x) {
@@ -155,7 +165,16 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const uint4* __restric
     const int row = send_base[e] + static_cast<int>(p) - lstart[e];
     const uint4* src = x + static_cast<int64_t>(i / top_k) * row_vecs;
     uint4* out = static_cast<uint4*>(xr.p[d]) + static_cast<int64_t>(row) * row_vecs;
-    for (int64_t v = lane; v < row_vecs; v += 32) out[v] = src[v];
+    // 8 loads in flight per lane before the (remote) stores
+    for (int64_t v0 = lane; v0 < row_vecs; v0 += 32 * 8) {
+      uint4 buf[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (v0 + 32 * u < row_vecs) buf[u] = src[v0 + 32 * u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (v0 + 32 * u < row_vecs) out[v0 + 32 * u] = buf[u];
+    }
     if (lane == 0) {
       static_cast<float*>(wr.p[d])[row] = load_weight(tw, w_dtype, i);
       dst[i] = (d << 24) | row;
@@ -177,16 +196,29 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const int32_t* __restri
     float acc[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
-    for (int j = 0; j < top_k; ++j) {
-      const int code = dst[t * top_k + j];
-      if (code < 0) continue;
-      const int d = code >> 24, row = code & 0xFFFFFF;
-      const uint4 q = *(reinterpret_cast<const uint4*>(yr.p[d]) + static_cast<int64_t>(row) * vec_per_row + v);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    // slots in batches of 8: the route codes, then the rows, are loaded before
+    // any sum; the sum runs in slot order
+    for (int j0 = 0; j0 < top_k; j0 += 8) {
+      int code[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        acc[2 * c] += __uint_as_float(w[c] << 16);
-        acc[2 * c + 1] += __uint_as_float(w[c] & 0xFFFF0000u);
+      for (int u = 0; u < 8; ++u) code[u] = j0 + u < top_k ? dst[t * top_k + j0 + u] : -1;
+      uint4 q[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        q[u] = make_uint4(0, 0, 0, 0);
+        if (code[u] >= 0)
+          q[u] = *(reinterpret_cast<const uint4*>(yr.p[code[u] >> 24]) +
+                   static_cast<int64_t>(code[u] & 0xFFFFFF) * vec_per_row + v);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (code[u] < 0) continue;
+        const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          acc[2 * c] += __uint_as_float(w[c] << 16);
+          acc[2 * c + 1] += __uint_as_float(w[c] & 0xFFFF0000u);
+        }
       }
     }
     uint4 o;

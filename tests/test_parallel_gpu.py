@@ -1,6 +1,8 @@
 """Multi-GPU paths on real GPUs (NCCL over NVLink): the column-sharded linear
 and the expert-parallel MoE layer must reproduce the single-GPU results bit
-for bit.  Each world size is skipped on machines with fewer GPUs."""
+for bit.  World size 1 runs the native expert-parallel kernels (count, plan,
+dispatch, barrier, combine) with the rank as its own peer.  Each world size
+is skipped on machines with fewer GPUs."""
 
 import os
 import socket
@@ -91,7 +93,7 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_column_parallel_and_expert_parallel(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
