@@ -304,6 +304,17 @@ def bench_moe(soft, steps, warmup, device):
     return ms
 
 
+def bench_router(soft, steps, warmup, device):
+    """Device router on config 2's logits (T=4096 x E=128 FP32, top-8, renormalised);
+    64 rotating logit sets (128 MB) so consecutive steps miss the L2."""
+    g = torch.Generator(device=device).manual_seed(5)
+    sets = [(torch.randn(MOE["t"], MOE["e"], generator=g, device=device),) for _ in range(64)]
+    gs = graphs_for(lambda lg: soft.moe_router(lg, MOE["k"]), sets, torch.cuda.Stream())
+    ms = time_graphs(gs, steps, warmup)
+    del gs, sets
+    return ms
+
+
 def bench_w4a4(soft, steps, warmup, device):
     m, n, k = W4A4
     sets = []
@@ -458,6 +469,10 @@ def main():
         fm = moe_flops()
         extra["config2_moe_layer"] = {"ms": ms_m, "tokens_per_s": MOE["t"] / (ms_m * 1e-3), "tflops": fm / ms_m / 1e9,
                                       "frac_bf16": fm / ms_m / 1e9 / pk["bf16_tflops"], "launches_per_step": 6}
+        ms_r = bench_router(soft, 256, 64, device)
+        rbytes = MOE["t"] * MOE["e"] * 4 + MOE["t"] * MOE["k"] * 8
+        extra["config2_router"] = {"ms": ms_r, "us": ms_r * 1e3, "gbs": rbytes / ms_r / 1e6,
+                                   "what": "softmax + top-8 + renormalise over 128 expert logits, 4096 tokens"}
         ms_w = bench_w4a4(soft, 50, 5, device)
         fw = 2.0 * W4A4[0] * W4A4[1] * W4A4[2]
         extra["config3_w4a4"] = {"ms": ms_w, "tflops": fw / ms_w / 1e9,

@@ -116,6 +116,18 @@ int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const vo
                     int out_dtype, int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* MoE router: for each of num_tokens tokens, softmax (FP32) over the          */
+/* num_experts logits [num_tokens, num_experts] (F32, BF16 or F16, dense),     */
+/* then the top_k largest probabilities in descending order (equal values:     */
+/* the lower expert first), renormalised to sum to one when renormalize != 0. */
+/* Writes topk_weights [num_tokens, top_k] (F32) and topk_ids (I32).  This is  */
+/* the routing vLLM computes before calling the reference adapter's            */
+/* _moe_apply (vllm:233), which receives it as topk_weights / topk_ids; the    */
+/* reference module has no router.  num_experts <= 256, top_k <= 32.           */
+int mxfp4_moe_router(const void* logits, int logits_dtype, int64_t num_tokens, int num_experts,
+                     int top_k, int renormalize, float* topk_weights, int32_t* topk_ids,
+                     void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* K4 -- device routing.  Replaces _make_routing (vllm:119-146) without its  */
 /* host sync.  Route r = t*top_k + j of topk_ids[num_tokens, top_k] (I32 or  */

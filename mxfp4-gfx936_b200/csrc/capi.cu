@@ -743,6 +743,25 @@ int mxfp4_peer_barrier(int32_t* const* flags, int rank, int world, int32_t* coun
   return MXFP4_OK;
 }
 
+int mxfp4_moe_router(const void* logits, int logits_dtype, int64_t num_tokens, int num_experts, int top_k,
+                     int renormalize, float* topk_weights, int32_t* topk_ids, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(logits_dtype == MXFP4_DTYPE_F32 || logits_dtype == MXFP4_DTYPE_BF16 || logits_dtype == MXFP4_DTYPE_F16,
+           "router logits must be F32, BF16 or F16");
+  MX_CHECK(num_tokens >= 0, "negative num_tokens");
+  MX_CHECK(num_experts >= 1 && num_experts <= 32 * kRouterPerLane, "num_experts must be in [1, 256]");
+  MX_CHECK(top_k >= 1 && top_k <= 32 && top_k <= num_experts, "top_k must be in [1, min(32, num_experts)]");
+  if (num_tokens == 0) return MXFP4_OK;
+  MX_CHECK(logits && topk_weights && topk_ids, "null pointer");
+  const int64_t blocks = (num_tokens + 7) / 8;  // 8 warps, one token each
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(info.sms) * 16)));
+  router_kernel<<<grid, 256, 0, as_stream(stream)>>>(logits, logits_dtype, num_tokens, num_experts, top_k,
+                                                       renormalize, topk_weights, topk_ids);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
 int64_t mxfp4_moe_route_capacity(int64_t num_routes, int num_experts, int block_m) {
   if (num_routes < 0 || num_experts <= 0 || block_m <= 0) return 0;
   return route_capacity(num_routes, num_experts, block_m);

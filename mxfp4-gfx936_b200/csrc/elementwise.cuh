@@ -299,4 +299,86 @@ __global__ void __launch_bounds__(256) combine_topk_kernel(const __nv_bfloat16* 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Router: per token, softmax over the experts' logits (FP32, max subtracted),
+// the top_k largest probabilities in descending order (equal values: the lower
+// expert first), optionally renormalised to sum to one.  This is the routing
+// the vLLM adapter receives in topk_weights / topk_ids.  One warp per token;
+// lane l holds the logits of experts l, l + 32, ... (E <= 32 * kRouterPerLane).
+// ---------------------------------------------------------------------------
+constexpr int kRouterPerLane = 8;  // E <= 256
+
+__device__ __forceinline__ float load_logit(const void* p, int dtype, int64_t i) {
+  if (dtype == MXFP4_DTYPE_F32) return static_cast<const float*>(p)[i];
+  if (dtype == MXFP4_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+__global__ void __launch_bounds__(256) router_kernel(const void* __restrict__ logits, int dtype, int64_t num_tokens,
+                                                     int num_experts, int top_k, int renormalize,
+                                                     float* __restrict__ w_out, int32_t* __restrict__ id_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; t < num_tokens; t += warps) {
+    float v[kRouterPerLane];
+#pragma unroll
+    for (int j = 0; j < kRouterPerLane; ++j) {
+      const int e = lane + 32 * j;
+      v[j] = e < num_experts ? load_logit(logits, dtype, t * num_experts + e) : -INFINITY;
+    }
+    float m = v[0];
+#pragma unroll
+    for (int j = 1; j < kRouterPerLane; ++j) m = fmaxf(m, v[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kRouterPerLane; ++j) {
+      v[j] = lane + 32 * j < num_experts ? expf(v[j] - m) : 0.0f;
+      sum += v[j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+#pragma unroll
+    for (int j = 0; j < kRouterPerLane; ++j) v[j] = v[j] / sum;  // probabilities; 0 beyond E
+    uint32_t taken = 0;
+    float my_w = 0.0f;
+    int my_id = 0;
+    for (int r = 0; r < top_k; ++r) {
+      float bv = -1.0f;
+      int bi = 0x7FFFFFFF;
+#pragma unroll
+      for (int j = 0; j < kRouterPerLane; ++j) {
+        const int e = lane + 32 * j;
+        if (e < num_experts && !(taken & (1u << j)) && v[j] > bv) {
+          bv = v[j];
+          bi = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      const bool found = bi < num_experts;  // false only when no candidate compares (NaN logits)
+      if (found && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+      if (lane == r) {
+        my_w = found ? bv : 0.0f;
+        my_id = found ? bi : -1;  // -1: no expert; the MoE ops drop such routes
+      }
+    }
+    float sel = lane < top_k ? my_w : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sel += __shfl_xor_sync(0xFFFFFFFFu, sel, o);
+    if (lane < top_k) {
+      w_out[t * top_k + lane] = renormalize ? my_w / sel : my_w;
+      id_out[t * top_k + lane] = my_id;
+    }
+  }
+}
+
 }  // namespace mx

@@ -101,6 +101,7 @@ _SIGNATURES = {
         [_VP, _INT, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64, _INT, _VP, _SZ, _VP],
     ),
     "mxfp4_quantize": (_INT, [_VP, _INT, _I64, _I64, _I64, _VP, _VP, _VP]),
+    "mxfp4_moe_router": (_INT, [_VP, _INT, _I64, _INT, _INT, _INT, _VP, _VP, _VP]),
     "mxfp4_gemm_w4a4_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "mxfp4_gemm_w4a4": (_INT, [_VP, _VP, _VP, _VP, _VP, _INT, _I64, _I64, _I64, _VP, _SZ, _VP]),
     "mxfp4_moe_route_capacity": (_I64, [_I64, _INT, _INT]),
@@ -461,6 +462,30 @@ def moe_route(topk_ids: torch.Tensor, num_experts: int, block_m: int = _BLOCK_M,
             _ptr(tid), _DTYPE_CODES[tid.dtype], t, k, num_experts, expert_offset, block_m,
             _ptr(sorted_ids), _ptr(expert_ids), _ptr(post), cap, _ptr(ws), ws_bytes, _stream(device)))
     return sorted_ids[:cap], expert_ids[: cap // block_m], post
+
+
+def moe_router(router_logits: torch.Tensor, top_k: int, renormalize: bool = True):
+    """Softmax top-k routing on the device: the ``topk_weights`` (float32) and
+    ``topk_ids`` (int32), both ``[M, top_k]``, that vLLM hands the adapter's
+    ``_moe_apply`` (vllm:233).  Probabilities are an FP32 softmax over the
+    experts; the top ``top_k`` come in descending order (equal values: the
+    lower expert first) and, with ``renormalize``, are rescaled to sum to one.
+    At most 256 experts and ``top_k <= min(32, experts)``."""
+    if router_logits.ndim != 2:
+        raise ValueError("router_logits must be 2-D [tokens, experts]")
+    if router_logits.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise TypeError(f"router_logits must be float32, bfloat16 or float16, got {router_logits.dtype}")
+    t, e = router_logits.shape
+    if not 1 <= top_k <= min(32, e) or e > 256:
+        raise ValueError(f"need 1 <= top_k <= min(32, experts) and experts <= 256, got top_k={top_k}, experts={e}")
+    device = _require_cuda(router_logits)
+    weights = torch.empty((t, top_k), dtype=torch.float32, device=device)
+    ids = torch.empty((t, top_k), dtype=torch.int32, device=device)
+    logits = _dense(router_logits)
+    with torch.cuda.device(device):
+        _check(_load_library().mxfp4_moe_router(_ptr(logits), _DTYPE_CODES[logits.dtype], t, e, top_k,
+                                                int(bool(renormalize)), _ptr(weights), _ptr(ids), _stream(device)))
+    return weights, ids
 
 
 def moe_layer_mxfp4(x: torch.Tensor, w13: torch.Tensor, w13_scale: torch.Tensor, w2: torch.Tensor,
