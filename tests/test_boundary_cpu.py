@@ -152,3 +152,20 @@ def test_unknown_backend_rejected_by_ops(monkeypatch):
     with pytest.raises(ValueError, match="unknown B200 MXFP4 backend"):
         soft.linear_mxfp4_soft(torch.zeros(2, 128, dtype=torch.bfloat16),
                                torch.zeros(64, 64, dtype=torch.uint8), torch.zeros(64, 4, dtype=torch.uint8))
+
+
+def test_router_argument_checks_on_cpu():
+    # the router rejects bad shapes, dtypes and sizes before it needs a GPU
+    soft = soft_module()
+    with pytest.raises(ValueError):
+        soft.moe_router(torch.randn(8), 2)
+    with pytest.raises(TypeError):
+        soft.moe_router(torch.randn(4, 8, dtype=torch.float64), 2)
+    with pytest.raises(ValueError):
+        soft.moe_router(torch.randn(4, 300), 2)
+    with pytest.raises(ValueError):
+        soft.moe_router(torch.randn(4, 8), 9)
+    with pytest.raises(ValueError):
+        soft.moe_router(torch.randn(4, 64), 33)
+    with pytest.raises(RuntimeError, match="no CPU path|sm_100"):
+        soft.moe_router(torch.randn(4, 8), 2)  # valid arguments, but no CPU path
