@@ -13,7 +13,8 @@ inputs resident in HBM, timed with CUDA events on the launching stream over
 exactly K steps (CUDA-graph replays rotating 4 input sets of 64 MB each, so
 the working set of consecutive steps exceeds the 126 MB L2).  ``e2e`` times the
 same metric through the public operator call with pinned HOST buffers (the
-activation copy in, the output copy out, every step).
+activation copy in, the output copy out, every step; consecutive steps are
+pipelined over upload, compute and download streams).
 
 At N=1 the other BASELINE configurations are measured as ``extra`` entries
 (o_proj, the decode sweep, the safe mode, the MoE layer of config 2).  With
@@ -256,27 +257,52 @@ DECODE_ONCE_ROW_BLOCKS = 6  # mirrors kDecodeOnceRowBlocks in csrc/capi.cu
 
 
 def bench_e2e_linear(soft, shape, steps, warmup, device):
+    """The public call with host buffers: every step copies its activations in
+    from pinned host memory, runs ``linear_mxfp4_soft`` and copies the whole
+    result back.  Steps are pipelined over three streams (upload, compute,
+    download) the way a serving loop overlaps requests, so step i's download
+    runs beside step i+1's upload over the full-duplex host link; events order
+    every reuse of the two device input buffers and of the result."""
     m, n, k = shape
     set_backend("fused")
     x, w, s = make_linear_inputs(m, n, k, 123, device)
     x_host = x.cpu().pin_memory()
     y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+    xd = [torch.empty_like(x), torch.empty_like(x)]
+    s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_used = [torch.cuda.Event(), torch.cuda.Event()]  # the GEMM that read xd[b] is done
+    del x
 
-    def step():
-        xd = x_host.to(device, non_blocking=True)
-        y = soft.linear_mxfp4_soft(xd, w, s)
-        y_host.copy_(y, non_blocking=True)
+    def step(i):
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_used[b])
+            xd[b].copy_(x_host, non_blocking=True)
+            ev_in[b].record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(ev_in[b])
+            y = soft.linear_mxfp4_soft(xd[b], w, s)
+            ev_used[b].record(s_comp)
+            done = torch.cuda.Event()
+            done.record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            y_host.copy_(y, non_blocking=True)
+            y.record_stream(s_out)
 
-    for _ in range(warmup):
-        step()
+    for i in range(warmup):
+        step(i)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
-        step()
-    end.record()
+    start.record(s_in)
+    for i in range(steps):
+        step(i)
+    s_in.wait_stream(s_out)
+    end.record(s_in)
     end.synchronize()
+    torch.cuda.synchronize()
     wall = (time.perf_counter() - t0) * 1e3 / steps
     ms = start.elapsed_time(end) / steps
     return max(ms, wall), x_host.numel() * 2, y_host.numel() * 2
