@@ -644,27 +644,59 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
     t_nvlink = ag_bytes / (NVLINK_GBS * 1e9)
     t_roof = max(t_tensor, t_nvlink)
 
-    # end to end: pinned host activations in, gathered output back to the host
+    # end to end: pinned host activations in on every rank, the gathered output
+    # (identical on every rank) read back once, by rank 0.  Steps are pipelined
+    # over upload, compute and download streams.  The layer's output buffers
+    # alternate and peers write into them, so rank 0's compute of step i+1 waits
+    # for its download of step i: the device barrier that ends step i+1 then
+    # holds every rank's step i+2 (which writes that buffer again) until the
+    # download is done.
     x_host = sets[0][0].cpu().pin_memory()
     y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
     layer0 = sets[0][1]
+    xd = [torch.empty_like(sets[0][0]), torch.empty_like(sets[0][0])]
+    s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_used = [torch.cuda.Event(), torch.cuda.Event()]
+    last_d2h = [None]
 
-    def e2e_step():
-        xd = x_host.to(device, non_blocking=True)
-        y_host.copy_(layer0(xd), non_blocking=True)
+    def e2e_step(i):
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_used[b])
+            xd[b].copy_(x_host, non_blocking=True)
+            ev_in[b].record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(ev_in[b])
+            if last_d2h[0] is not None:
+                s_comp.wait_event(last_d2h[0])
+            y = layer0(xd[b])
+            ev_used[b].record(s_comp)
+            done = torch.cuda.Event()
+            done.record(s_comp)
+        if rank == 0:
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                y_host.copy_(y, non_blocking=True)
+                d2h = torch.cuda.Event()
+                d2h.record(s_out)
+                last_d2h[0] = d2h
 
-    for _ in range(args.warmup):
-        e2e_step()
+    for i in range(args.warmup):
+        e2e_step(i)
     torch.cuda.synchronize()
     barrier()
     e_steps = max(10, args.steps // 4)
     st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
-    st.record()
-    for _ in range(e_steps):
-        e2e_step()
-    en.record()
+    st.record(s_in)
+    for i in range(e_steps):
+        e2e_step(i)
+    s_in.wait_stream(s_comp)
+    s_in.wait_stream(s_out)
+    en.record(s_in)
     en.synchronize()
+    torch.cuda.synchronize()
     wall = (time.perf_counter() - t0) * 1e3 / e_steps
     e2e_ms = _max_over_ranks(max(st.elapsed_time(en) / e_steps, wall), device)
     barrier()
