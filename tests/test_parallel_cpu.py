@@ -1,5 +1,8 @@
 """Multi-rank host logic on CPU (gloo, world size 2): the column-sharded
-linear's shard split and all-gather interleave give the unsharded result."""
+linear's shard split and all-gather interleave give the unsharded result; its
+choice between NVSwitch multicast and CUDA IPC output buffers is made by group
+size and agreed by every rank; the expert-parallel exchange reproduces the
+single layer."""
 
 import os
 import socket
@@ -118,3 +121,80 @@ def test_expert_range_and_topk_sum():
     want = (rows.view(2, 3, 16).float()[:, 0] + rows.view(2, 3, 16).float()[:, 1]
             + rows.view(2, 3, 16).float()[:, 2]).to(torch.bfloat16)
     assert torch.equal(s.view(torch.int16), want.view(torch.int16))
+
+
+def _multicast_policy_worker(rank, world, port, q):
+    # the column-parallel layer's choice between NVSwitch multicast buffers and
+    # CUDA IPC peer buffers, with both kinds of buffer faked: the choice is made
+    # by group size, and collectively (one rank without multicast -> none use it)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cp = load_by_path("mxfp4_column_parallel", PKG / "column_parallel.py")
+        pm = cp._peer_memory()
+        made = []
+
+        class FakeIpc:
+            def __init__(self, shape, dtype, group):
+                made.append("ipc")
+
+        class FakeSymm:
+            multicast_ptr = 1
+
+        supported = {"value": True}
+
+        def fake_create(shape, dtype, device, group):
+            made.append("symm-try")
+            return FakeSymm() if supported["value"] else None
+
+        pm.PeerBuffers = FakeIpc
+        cp._SymmBuffer.create = staticmethod(fake_create)
+        w = torch.zeros(32, 16, dtype=torch.uint8)
+        s = torch.zeros(32, 1, dtype=torch.uint8)
+        out = {}
+        # group of 2 GPUs, default policy: IPC peer buffers, multicast not tried
+        made.clear()
+        layer = cp.ColumnParallelLinear(w, s, 32 * world, rank, world, fused=True)
+        bufs = layer._alloc(4, torch.bfloat16, "cpu")
+        out["two"] = (made.copy(), type(bufs[0]).__name__)
+        # a layer of 8 ranks (as it sees its group): multicast buffers
+        made.clear()
+        layer = cp.ColumnParallelLinear(w, s, 32 * 8, rank, 8, fused=True)
+        bufs = layer._alloc(4, torch.bfloat16, "cpu")
+        out["eight"] = (made.copy(), type(bufs[0]).__name__)
+        # forced multicast, one rank without support: every rank raises
+        made.clear()
+        supported["value"] = rank == 0
+        layer = cp.ColumnParallelLinear(w, s, 32 * world, rank, world, fused=True, multicast=True)
+        try:
+            layer._alloc(4, torch.bfloat16, "cpu")
+            out["forced"] = "no error"
+        except RuntimeError:
+            out["forced"] = "raised"
+        # default policy at 8, one rank without support: every rank falls back to IPC
+        made.clear()
+        layer = cp.ColumnParallelLinear(w, s, 32 * 8, rank, 8, fused=True)
+        bufs = layer._alloc(4, torch.bfloat16, "cpu")
+        out["fallback"] = type(bufs[0]).__name__
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_column_parallel_multicast_policy_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_multicast_policy_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    res = dict(q.get(timeout=5) for _ in procs)
+    assert all(p.exitcode == 0 for p in procs)
+    for rank in (0, 1):
+        out = res[rank]
+        assert out["two"] == (["ipc", "ipc"], "FakeIpc"), out
+        assert out["eight"] == (["symm-try", "symm-try"], "FakeSymm"), out
+        assert out["forced"] == "raised", out
+        assert out["fallback"] == "FakeIpc", out
