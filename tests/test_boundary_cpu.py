@@ -9,6 +9,7 @@ the reference's exception type before any device work.
 import ctypes
 import re
 
+import numpy as np
 import pytest
 import torch
 
@@ -169,3 +170,28 @@ def test_router_argument_checks_on_cpu():
         soft.moe_router(torch.randn(4, 64), 33)
     with pytest.raises(RuntimeError, match="no CPU path|sm_100"):
         soft.moe_router(torch.randn(4, 8), 2)  # valid arguments, but no CPU path
+
+
+def _padded_rows(counts, block):
+    return int(sum(-(-int(c) // block) * block for c in counts))
+
+
+def test_routing_and_ep_capacities_hold_every_layout():
+    # the capacities size device buffers before the routes are known: they must
+    # hold the padded layout of any distribution of the routes over the experts
+    lib = soft._load_library()
+    rng = np.random.default_rng(0)
+    for routes, experts, block in [(32768, 128, 128), (4096, 64, 256), (7, 3, 128), (0, 8, 64), (100, 1, 256)]:
+        cap = lib.mxfp4_moe_route_capacity(routes, experts, block)
+        assert cap % block == 0
+        for dist_ in (rng.multinomial(routes, np.ones(experts) / experts), np.eye(experts, dtype=int)[0] * routes):
+            assert _padded_rows(dist_, block) <= cap
+    for t, k, e, world in [(512, 8, 128, 8), (2048, 8, 128, 2), (1, 1, 4, 4), (300, 4, 32, 1)]:
+        cap = lib.mxfp4_ep_moe_recv_capacity(t, k, e, world)
+        assert cap % 256 == 0
+        el = e // world
+        # worst case for one owner: every route of every rank lands on its experts
+        for dist_ in (rng.multinomial(world * t * k, np.ones(el) / el), np.eye(el, dtype=int)[0] * world * t * k):
+            assert _padded_rows(dist_, 256) <= cap
+    assert lib.mxfp4_ep_moe_recv_capacity(10, 2, 10, 4) == 0  # experts must divide over the ranks
+    assert lib.mxfp4_ep_moe_recv_capacity(-1, 2, 8, 4) == 0
