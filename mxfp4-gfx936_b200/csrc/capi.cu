@@ -221,8 +221,9 @@ int launch_gemv(const GemvParams& g, int sms, cudaStream_t stream) {
   return go(mxfp4_gemv_kernel<2, BMODE, FP16>);
 }
 
-// The kernels take one E8M0 scale per 32 K in row-major [rows, K/32] and walk K in
-// stages of 64 codes, two scale words at a time: K must be a positive multiple of 128.
+// The kernels take one E8M0 scale per 32 K in row-major [rows, K/32] and read the
+// scales as 32-bit words of four (128 K, two 64-code stages): K must be a positive
+// multiple of 128.
 int check_scales_layout(int64_t k) {
   if (k <= 0 || k % 128 != 0)
     return fail(MXFP4_ERR_INVALID_ARGUMENT, "logical K must be a positive multiple of 128, got " + std::to_string(k));
