@@ -7,8 +7,10 @@ Headline workload (the large-prefill dense linear):
 qkv_proj M=4096, K=2048, N=5120 through the fused W4A16 backend.  With 16
 row blocks of 256 it decodes each weight element once (the decode kernel
 into an L2-resident BF16 copy, then the TMA-fed pair GEMM: two launches per
-step); ``roofline`` is the GEMM's, from the step time minus the separately
-timed decode kernel.  A "step" is one pass of the linear over one batch.  ``value`` is the whole-job TFLOP/s (2*M*N*K per step) with the
+step); ``roofline`` is the GEMM launch's own, timed with CUDA events around
+graph replays of that launch alone (``mxfp4_linear_dequantized`` on decoded
+weight sets, the second launch of the step).  A "step" is one pass of the
+linear over one batch.  ``value`` is the whole-job TFLOP/s (2*M*N*K per step) with the
 inputs resident in HBM, timed with CUDA events on the launching stream over
 exactly K steps (CUDA-graph replays rotating 4 input sets of 64 MB each, so
 the working set of consecutive steps exceeds the 126 MB L2).  ``e2e`` times the
@@ -28,6 +30,16 @@ all-gather bytes at the measured NVLink rate.  The same linear with an NCCL
 all-gather, and the expert-parallel MoE layer of config 2 (T/G tokens and E/G
 experts per rank; native peer-memory dispatch and combine, and the NCCL
 all-to-all path) are ``extra`` entries.
+
+``cpu_baseline`` is the reference's safe path restated with PyTorch CPU ops
+(oracle/ref_cpu.py) on the host cores for the headline workload;
+``cpu_baselines`` adds configs 0 (M=64 linear), 2 (the MoE layer) and 3 (W4A4,
+dequant both + matmul) on bounded samples.  The tensor-core denominators are
+measured in the same run by libmxfp4_b200_probe.so (back-to-back BF16 and
+block-scaled FP4 MMAs on every SM, ``peaks_probe``); the FP4 fraction of
+config 3 is taken against that measured FP4 rate.  At N>1 every rank first
+checks the sharded linear and the expert-parallel layer bit for bit against
+the single-GPU calls on the same inputs (``parity``); a mismatch fails the run.
 
 ``--impl reference`` times the reference's safe path restated with PyTorch CPU
 ops (oracle/ref_cpu.py) on this machine's host cores for the same workload; the
@@ -253,6 +265,48 @@ def bench_decode_kernel(soft, shape, steps, warmup, device):
     return ms
 
 
+def bench_gemm_predecoded(soft, shape, steps, warmup, device):
+    """The GEMM launch of a decode-once step on its own: ``linear_dequantized``
+    on weights decoded beforehand, 4 rotating sets (x 16 MB, decoded W 21 MB,
+    y 42 MB each: the rotation exceeds the L2), CUDA events around replays."""
+    m, n, k = shape
+    sets = []
+    for i in range(4):
+        x, w, s = make_linear_inputs(m, n, k, i, device)
+        sets.append((x, soft.dequant_mxfp4(w, s, torch.bfloat16)))
+        del w, s
+    gs = graphs_for(lambda x, wd: soft.linear_dequantized(x, wd), sets, torch.cuda.Stream())
+    ms = time_graphs(gs, steps, warmup)
+    del gs, sets
+    return ms
+
+
+def probe_peaks():
+    """Dense tensor-core rates measured on this GPU by libmxfp4_b200_probe.so:
+    MMAs issued back to back from shared-memory operands on every SM (BF16
+    kind::f16 and block-scaled FP4 kind::mxf4, M=128 N=256); best of 3."""
+    import ctypes
+    lib = ctypes.CDLL(str(PKG / "libmxfp4_b200_probe.so"))
+    fn = lib.mxfp4_probe_mma_rate
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double),
+                   ctypes.c_void_p]
+    out = {}
+    stream = torch.cuda.current_stream().cuda_stream
+    for kind, name in ((0, "bf16_tflops"), (1, "fp4_tflops")):
+        best = 0.0
+        for _ in range(4):
+            ms, fl = ctypes.c_float(), ctypes.c_double()
+            rc = fn(kind, 20000, ctypes.byref(ms), ctypes.byref(fl), ctypes.c_void_p(stream))
+            if rc:
+                raise RuntimeError(f"tensor-core rate probe failed with status {rc}")
+            best = max(best, fl.value / (ms.value * 1e-3) / 1e12)
+        out[name] = best
+    out["what"] = ("tcgen05 MMAs back to back, operands in shared memory, one CTA per SM, M=128 N=256 "
+                   "(kind::f16 BF16 K=16; kind::mxf4.block_scale.block32 K=64), best of 4 x 80000 MMAs per SM")
+    return out
+
+
 DECODE_ONCE_ROW_BLOCKS = 6  # mirrors kDecodeOnceRowBlocks in csrc/capi.cu
 
 
@@ -330,6 +384,58 @@ def bench_moe(soft, steps, warmup, device):
     return ms
 
 
+def bench_e2e_moe(soft, steps, warmup, device):
+    """The MoE layer through its public call with host buffers: each step copies
+    x [T, H] BF16 and the routing (top-k weights F32, ids I64) in from pinned
+    host memory, runs ``moe_layer_mxfp4`` and copies the whole [T, H] result
+    back; steps pipelined over upload, compute and download streams as in the
+    linear's e2e."""
+    x, w13, s13, w2, s2, tw, tid = make_moe_inputs(device, seed=31, **MOE)
+    hosts = [t.cpu().pin_memory() for t in (x, tw, tid)]
+    out_host = torch.empty(MOE["t"], MOE["h"], dtype=torch.bfloat16).pin_memory()
+    dev_in = [[torch.empty_like(t) for t in (x, tw, tid)] for _ in range(2)]
+    del x, tw, tid
+    s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_used = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def step(i):
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_used[b])
+            for d, h in zip(dev_in[b], hosts):
+                d.copy_(h, non_blocking=True)
+            ev_in[b].record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(ev_in[b])
+            xd, twd, tidd = dev_in[b]
+            y = soft.moe_layer_mxfp4(xd, w13, s13, w2, s2, twd, tidd)
+            ev_used[b].record(s_comp)
+            done = torch.cuda.Event()
+            done.record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            out_host.copy_(y, non_blocking=True)
+            y.record_stream(s_out)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    for i in range(steps):
+        step(i)
+    s_in.wait_stream(s_out)
+    end.record(s_in)
+    end.synchronize()
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3 / steps
+    ms = max(start.elapsed_time(end) / steps, wall)
+    h2d = sum(h.numel() * h.element_size() for h in hosts)
+    return ms, h2d, out_host.numel() * 2
+
+
 def bench_router(soft, steps, warmup, device):
     """Device router on config 2's logits (T=4096 x E=128 FP32, top-8, renormalised);
     64 rotating logit sets (128 MB) so consecutive steps miss the L2."""
@@ -397,6 +503,62 @@ def cpu_linear_tflops(shape, steps, warmup, budget_s=25.0):
             "m_used": m_used, "threads": torch.get_num_threads()}
 
 
+def _time_cpu(fn, budget_s, min_steps=2, max_steps=10):
+    fn()  # warm-up
+    times = []
+    t_all = time.perf_counter()
+    while len(times) < max_steps and (len(times) < min_steps or time.perf_counter() - t_all < budget_s):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return sum(times) / len(times), len(times)
+
+
+def cpu_baselines(budget_s=8.0):
+    """The reference's safe path (torch-CPU port, all host threads) on
+    BASELINE configs 0, 2 and 3, each on a bounded sample of its workload."""
+    ref = _load("mxfp4_ref_cpu", ROOT / "oracle" / "ref_cpu.py")
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
+    out = {}
+    # config 0: the dense safe linear at M=64 (its full size)
+    m, n, k = 64, 5120, 2048
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = torch.randint(0, 256, (n, k // 2), generator=g, dtype=torch.uint8)
+    s = torch.randint(118, 131, (n, k // 32), generator=g, dtype=torch.uint8)
+    sec, steps = _time_cpu(lambda: ref.linear(x, w, s), budget_s)
+    out["config0_linear_m64"] = {"value": 2.0 * m * n * k / sec / 1e12, "unit": "TFLOP/s", "ms": sec * 1e3,
+                                 "cores": threads, "kind": "port", "sample": f"full config 0 ({m}x{n}x{k}), "
+                                 f"{steps} timed calls"}
+    # config 2: the MoE layer on a token sample (all 128 experts' weights)
+    t = 512
+    cfg = dict(MOE, t=t)
+    x, w13, s13, w2, s2, tw, tid = make_moe_inputs(torch.device("cpu"), seed=0, **cfg)
+    sec, steps = _time_cpu(lambda: ref.moe_layer(x, w13, s13, w2, s2, tw, tid), budget_s, max_steps=4)
+    out["config2_moe_layer"] = {"value": t / sec, "unit": "tokens/s", "ms": sec * 1e3, "cores": threads,
+                                "kind": "port", "tflops": moe_flops(cfg) / sec / 1e12,
+                                "sample": f"{t} of config 2's {MOE['t']} tokens, same experts and routing "
+                                          f"distribution, {steps} timed calls"}
+    del x, w13, s13, w2, s2, tw, tid
+    # config 3: W4A4 as the reference computes it (dequant both operands, BF16 matmul), on a row sample
+    m, n, k = 1024, W4A4[1], W4A4[2]
+    g = torch.Generator().manual_seed(3)
+    a = torch.randint(0, 256, (m, k // 2), generator=g, dtype=torch.uint8)
+    sa = torch.randint(118, 131, (m, k // 32), generator=g, dtype=torch.uint8)
+    b = torch.randint(0, 256, (n, k // 2), generator=g, dtype=torch.uint8)
+    sb = torch.randint(118, 131, (n, k // 32), generator=g, dtype=torch.uint8)
+
+    def w4a4():
+        return torch.matmul(ref.dequant(a, sa, torch.bfloat16), ref.dequant(b, sb, torch.bfloat16).T)
+
+    sec, steps = _time_cpu(w4a4, budget_s, max_steps=4)
+    out["config3_w4a4"] = {"value": 2.0 * m * n * k / sec / 1e12, "unit": "TFLOP/s", "ms": sec * 1e3,
+                           "cores": threads, "kind": "port",
+                           "sample": f"{m} of config 3's {W4A4[0]} rows ({m}x{n}x{k}), {steps} timed calls"}
+    return out
+
+
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
@@ -450,11 +612,13 @@ def main():
     ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "fused", device, sampler=sampler)
     flops = 2.0 * m * n * k
     tflops = flops / (ms * 1e-3) / 1e12
-    # decode-once (>= 6 row blocks): two launches per step, the decode kernel then the GEMM
+    # decode-once (>= 6 row blocks): two launches per step, the decode kernel then the GEMM;
+    # each launch is timed on its own with CUDA events around graph replays of it alone
     decode_once = (m + 255) // 256 >= DECODE_ONCE_ROW_BLOCKS
     dec_ms = bench_decode_kernel(soft, QKV, args.steps, args.warmup, device) if decode_once else 0.0
-    gemm_ms = ms - dec_ms
+    gemm_ms = bench_gemm_predecoded(soft, QKV, args.steps, args.warmup, device) if decode_once else ms
     gemm_tflops = flops / (gemm_ms * 1e-3) / 1e12
+    probe = probe_peaks()
     e2e_ms, h2d, d2h = bench_e2e_linear(soft, QKV, max(10, args.steps // 4), args.warmup, device)
 
     line = {
@@ -468,13 +632,17 @@ def main():
                      "frac": gemm_tflops / pk["bf16_tflops"], "traffic": profile_traffic("linear_fused_qkv"),
                      "peak_source": f"{pk_kind} bf16 burst",
                      "kernel": "pair GEMM (TMA-fed decoded weights)" if decode_once else "pair GEMM (decode in producer)",
-                     "kernel_ms": gemm_ms, "decode_kernel_ms": dec_ms,
+                     "kernel_ms": gemm_ms, "kernel_timing": "the GEMM launch alone: CUDA events around graph "
+                     "replays of mxfp4_linear_dequantized over 4 rotating decoded-weight sets",
+                     "frac_of_probe": gemm_tflops / probe["bf16_tflops"],
+                     "decode_kernel_ms": dec_ms,
                      "decode_kernel_gbs": (n * k // 2 + n * k // 32 + 2 * n * k) / (dec_ms * 1e6) if dec_ms else None,
                      "step_frac": tflops / pk["bf16_tflops"]},
         "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps * (2 if decode_once else 1),
         "clocks": sampler.result(),
+        "peaks_probe": probe,
     }
 
     if not args.no_extra:
@@ -493,8 +661,11 @@ def main():
                                           "tflops": 2.0 * dm * n * k / ms_d / 1e9}
         ms_m = bench_moe(soft, 20, 3, device)
         fm = moe_flops()
+        e2e_m, h2d_m, d2h_m = bench_e2e_moe(soft, 10, 3, device)
         extra["config2_moe_layer"] = {"ms": ms_m, "tokens_per_s": MOE["t"] / (ms_m * 1e-3), "tflops": fm / ms_m / 1e9,
-                                      "frac_bf16": fm / ms_m / 1e9 / pk["bf16_tflops"], "launches_per_step": 6}
+                                      "frac_bf16": fm / ms_m / 1e9 / pk["bf16_tflops"], "launches_per_step": 6,
+                                      "e2e": {"value": MOE["t"] / (e2e_m * 1e-3), "unit": "tokens/s", "ms": e2e_m,
+                                              "h2d_bytes_per_step": h2d_m, "d2h_bytes_per_step": d2h_m}}
         ms_r = bench_router(soft, 256, 64, device)
         rbytes = MOE["t"] * MOE["e"] * 4 + MOE["t"] * MOE["k"] * 8
         extra["config2_router"] = {"ms": ms_r, "us": ms_r * 1e3, "gbs": rbytes / ms_r / 1e6,
@@ -502,6 +673,8 @@ def main():
         ms_w = bench_w4a4(soft, 50, 5, device)
         fw = 2.0 * W4A4[0] * W4A4[1] * W4A4[2]
         extra["config3_w4a4"] = {"ms": ms_w, "tflops": fw / ms_w / 1e9,
+                                 "frac_fp4_measured": fw / ms_w / 1e9 / probe["fp4_tflops"],
+                                 "fp4_peak_measured": probe["fp4_tflops"],
                                  "frac_fp4_nominal": fw / ms_w / 1e9 / FP4_NOMINAL_TFLOPS,
                                  "vs_bf16_peak": fw / ms_w / 1e9 / pk["bf16_tflops"],
                                  "launches_per_step": 3}
@@ -511,6 +684,8 @@ def main():
     line["cpu_baseline"] = {"value": cb["tflops_mean"], "unit": "TFLOP/s", "cores": cb["threads"], "kind": "port",
                             "sample": f"qkv_proj {cb['m_used']}x{n}x{k}, 2 timed steps; reference safe path "
                                       "(dequant + torch.matmul) as torch CPU ops (oracle/ref_cpu.py)"}
+    if not args.no_extra:
+        line["cpu_baselines"] = cpu_baselines()
     status = soft.device_status()
     if status:
         line["device_status"] = status
@@ -565,6 +740,16 @@ def bench_ep_moe(soft, ep_mod, world, rank, device, steps, warmup, barrier, fuse
         layer = ep_mod.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, fused=fused)
         sets.append((x[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous(), layer))
         del w13, s13, w2, s2, x, tw, tid
+    # parity before timing: this rank's rows of the expert-parallel layer must
+    # equal, bit for bit, the single-GPU layer on the full input (set 0)
+    x, w13, s13, w2, s2, tw, tid = make_moe_inputs(device, seed=7, **MOE)
+    y_full = soft.moe_layer_mxfp4(x, w13, s13, w2, s2, tw, tid)[sl]
+    xs, tws, tids, layer = sets[0]
+    y_ep = layer(xs, tws, tids)
+    torch.cuda.synchronize()
+    parity_ok = bool(torch.equal(y_ep.view(torch.int16), y_full.view(torch.int16)))
+    del x, w13, s13, w2, s2, tw, tid, y_full, y_ep
+    barrier()
     ms = None
     timing = "eager"
     if fused:
@@ -596,7 +781,7 @@ def bench_ep_moe(soft, ep_mod, world, rank, device, steps, warmup, barrier, fuse
     # bytes a rank must receive over NVLink per step: dispatched rows from the
     # other ranks plus their combined rows coming back (uniform routing)
     nv_bytes = 2 * routes_local * (world - 1) / world * MOE["h"] * 2
-    return ms, nv_bytes, moe_flops(), timing
+    return ms, nv_bytes, moe_flops(), timing, parity_ok
 
 
 def run_sharded(args, soft, world, rank, device, pk, pk_kind):
@@ -620,6 +805,17 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
         shard_sets.append((x, layer.w, layer.s))
         nccl_sets.append((x, cp.ColumnParallelLinear(layer.w, layer.s, n, rank, world)))
         del w, s
+    # parity before timing: the fused sharded linear and the NCCL path against
+    # the single-GPU linear on the full weight (set 0), bit for bit, on every rank
+    xw, ww, sw = make_linear_inputs(m, n, k, 0, device)
+    y_1 = soft.linear_mxfp4_soft(xw, ww, sw)
+    y_tp = sets[0][1](xw)
+    tp_ok = bool(torch.equal(y_tp.view(torch.int16), y_1.view(torch.int16)))
+    y_nccl = nccl_sets[0][1](xw)
+    tp_nccl_ok = bool(torch.equal(y_nccl.view(torch.int16), y_1.view(torch.int16)))
+    torch.cuda.synchronize()
+    del xw, ww, sw, y_1, y_tp, y_nccl
+    barrier()
     # the shard GEMM alone (the dominant kernel), then GEMM + all-gather
     gs_local = graphs_for(lambda x, w, s: soft.linear_mxfp4_soft(x, w, s), shard_sets, torch.cuda.Stream())
     ms_gemm = _max_over_ranks(time_graphs(gs_local, args.steps, args.warmup, barrier=barrier), device)
@@ -704,10 +900,15 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
 
     # expert-parallel MoE layer (config 2, tokens data-parallel across ranks)
     ep_steps = max(5, min(20, args.steps // 10))
-    ms_ep, ep_nv_bytes, fm, ep_timing = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup,
-                                                     barrier)
-    ms_ep_nccl, _, _, _ = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup, barrier,
-                                       fused=False)
+    ms_ep, ep_nv_bytes, fm, ep_timing, ep_ok = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps,
+                                                            args.warmup, barrier)
+    ms_ep_nccl, _, _, _, ep_nccl_ok = bench_ep_moe(soft, ep_mod, world, rank, device, ep_steps, args.warmup, barrier,
+                                                   fused=False)
+    # parity of every rank: the minimum over ranks of each check
+    flags = torch.tensor([tp_ok, tp_nccl_ok, ep_ok, ep_nccl_ok], dtype=torch.int32, device=device)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    parity = {"tp": bool(flags[0]), "tp_nccl": bool(flags[1]), "ep": bool(flags[2]), "ep_nccl": bool(flags[3]),
+              "what": "each rank's output vs the single-GPU call on the same inputs, bit for bit, min over ranks"}
     t_ep_roof = max(fm / world / (pk["bf16_tflops"] * 1e12), ep_nv_bytes / (NVLINK_GBS * 1e9))
     status = soft.device_status()
     status = int(_max_over_ranks(float(status), device))
@@ -734,6 +935,7 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
                     "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2},
             "gpu_launches": args.steps * 3,
             "clocks": sampler.result(),
+            "parity": parity,
             "extra": {"tp_nccl_allgather": {"ms": ms_nccl, "tflops": flops / (ms_nccl * 1e-3) / 1e12,
                                             "what": "shard GEMM then NCCL all_gather_into_tensor + interleave"},
                       "config2_moe_layer_ep": {
@@ -752,6 +954,10 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
         print(json.dumps(line), flush=True)
     barrier()
     dist.destroy_process_group()
+    if not all(parity[key] for key in ("tp", "tp_nccl", "ep", "ep_nccl")):
+        if rank == 0:
+            print("parity check failed: a multi-GPU result differs from the single-GPU call", file=sys.stderr)
+        return 1
     return 0
 
 

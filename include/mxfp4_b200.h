@@ -93,6 +93,17 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
                        int64_t m, int64_t n, int64_t k, int mode, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* The matmul half of the safe path (soft:372-373) on weights already       */
+/* decoded by mxfp4_dequant: out = round(x . w_deq^T) (+ bias), w_deq [n, k] */
+/* in x's dtype with row pitch ldw ELEMENTS (16-byte aligned).  The same    */
+/* kernels and summation order as mxfp4_linear_w4a16, so a dequant followed */
+/* by this call gives that call's bits; it is also the second launch of a  */
+/* decode-once fused linear, timed on its own by the benchmark.  No         */
+/* workspace.                                                               */
+int mxfp4_linear_dequantized(const void* x, int x_dtype, int64_t ldx, const void* w_deq, int64_t ldw,
+                             const void* bias, void* out, int64_t ldo, int64_t m, int64_t n, int64_t k,
+                             void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Quantizer -- BF16/F32 -> packed MXFP4 + E8M0 (the W4A4 configuration's   */
 /* OCP rounding; the reference only has a test quantizer, test:28-60).       */
@@ -152,7 +163,10 @@ int mxfp4_moe_route(const void* topk_ids, int ids_dtype, int64_t num_tokens, int
 /* (then * topk_weights[t, j] and rounded again if mul_routed_weight) for    */
 /* e = topk_ids[t, j] in [0, num_experts); other routes leave C[t, j, :] = 0.*/
 /* A' = A in C's dtype, or dequant(A, a_mx_scale) when a_dtype is U8 (W4A4,  */
-/* soft:468-475).  Rounding is to c_dtype (F32, BF16 or F16).                */
+/* soft:468-475).  Rounding is to c_dtype (F32, BF16 or F16).  With C F32    */
+/* the products are those of an FP32 matmul (soft:405): A is split exactly   */
+/* into BF16 parts (one for BF16 or U8 A, two for F16, three for F32), each  */
+/* part times the exactly decoded weights, FP32 accumulation.               */
 /* A: [num_tokens, k] (a_dtype BF16/F16/F32, or U8 packed [num_tokens, k/2]  */
 /* with a_mx_scale [num_tokens, k/32]); B: [num_experts, n, k/2] u8;         */
 /* B_mx: [num_experts, n, k/32] u8; a_scale: 1 FP32; b_scale: [num_experts]  */
@@ -251,9 +265,24 @@ int mxfp4_ipc_free(void* ptr);
 /* all flag arrays start at zero.  counter: a local device int32, zero     */
 /* before the first call, advanced by one per call.  Orders this rank's     */
 /* earlier stores (including stores into peers' memory) before the signal.  */
-/* Every rank makes the same sequence of calls.  A wait longer than about   */
-/* 2 s records MXFP4_ERR_TIMEOUT in the device status word and returns.     */
+/* Every rank makes the same sequence of calls.  A wait longer than 2 s     */
+/* records MXFP4_ERR_TIMEOUT in the device status word and returns.         */
 int mxfp4_peer_barrier(int32_t* const* flags, int rank, int world, int32_t* counter, void* stream);
+
+/* The same barrier with its wait limit given in microseconds (0: 2 s; at   */
+/* most 60 s).  No counterpart in the reference.                            */
+int mxfp4_peer_barrier_timed(int32_t* const* flags, int rank, int world, int32_t* counter,
+                             int64_t timeout_us, void* stream);
+
+/* After a barrier recorded MXFP4_ERR_TIMEOUT the ranks' epochs disagree:    */
+/* this rank's counter advanced while a peer's signal is missing, so later  */
+/* barriers could pass early or keep timing out.  Reset before reuse, on    */
+/* every rank: wait until no barrier kernel of any rank is running (each    */
+/* rank synchronises its device, then a host-side barrier of the group),    */
+/* call this to zero the local flag array [world] and the counter, wait for */
+/* it on every rank (synchronise, host barrier again), then resume.  No     */
+/* counterpart in the reference.                                            */
+int mxfp4_peer_barrier_reset(int32_t* local_flags, int world, int32_t* counter, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Expert-parallel MoE layer.  No counterpart in the reference;             */

@@ -4,7 +4,9 @@
 
 The library is one translation unit (csrc/capi.cu includes every kernel
 header) compiled for ``sm_100a`` only; the CUDA runtime is linked statically,
-so the .so depends only on the driver at run time.
+so the .so depends only on the driver at run time.  The benchmark's
+tensor-core rate probe (csrc/probe_mma.cu) is built beside it as
+libmxfp4_b200_probe.so.
 """
 
 from __future__ import annotations
@@ -18,7 +20,12 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "libmxfp4_b200.so"
 SOURCES = [HERE / "csrc" / "capi.cu"]
-DEPS = sorted((HERE / "csrc").glob("*.cu*")) + [HERE.parent / "include" / "mxfp4_b200.h"]
+DEPS = sorted((HERE / "csrc").glob("*.cuh")) + [HERE / "csrc" / "capi.cu", HERE.parent / "include" / "mxfp4_b200.h"]
+# the tensor-core rate probe the benchmark reads its FP4 denominator from (not
+# part of the operator library)
+PROBE_LIB = HERE / "libmxfp4_b200_probe.so"
+PROBE_SOURCES = [HERE / "csrc" / "probe_mma.cu"]
+PROBE_DEPS = sorted((HERE / "csrc").glob("*.cuh")) + PROBE_SOURCES + [HERE.parent / "include" / "mxfp4_b200_probe.h"]
 
 
 def nvcc() -> str:
@@ -39,25 +46,31 @@ def flags(verbose: bool = False) -> list[str]:
     return f
 
 
-def up_to_date() -> bool:
-    if not LIB.is_file():
+def up_to_date(lib: Path = LIB, deps=DEPS) -> bool:
+    if not lib.is_file():
         return False
-    t = LIB.stat().st_mtime
-    return all(d.stat().st_mtime <= t for d in DEPS)
+    t = lib.stat().st_mtime
+    return all(d.stat().st_mtime <= t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and up_to_date():
-        return LIB
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *flags(verbose), "-o", str(tmp), *map(str, SOURCES)]
+def _compile(lib: Path, sources, verbose: bool) -> None:
+    tmp = lib.with_suffix(".so.tmp")
+    cmd = [nvcc(), *flags(verbose), "-o", str(tmp), *map(str, sources)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
         raise RuntimeError(f"nvcc failed ({res.returncode}): {' '.join(cmd)}")
     if verbose:
         sys.stdout.write(res.stderr)
-    os.replace(tmp, LIB)
+    os.replace(tmp, lib)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Build the operator library and the rate probe; returns the former."""
+    if force or not up_to_date(PROBE_LIB, PROBE_DEPS):
+        _compile(PROBE_LIB, PROBE_SOURCES, verbose)
+    if force or not up_to_date():
+        _compile(LIB, SOURCES, verbose)
     return LIB
 
 

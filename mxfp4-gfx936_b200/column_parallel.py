@@ -173,7 +173,7 @@ class ColumnParallelLinear:
         x2 = soft._dense(x2)
         device = x2.device
         backend = soft._backend()
-        mode = soft._LINEAR_FUSED if backend == "fused" else soft._LINEAR_SAFE
+        mode = soft._LINEAR_FUSED if backend in soft._FUSED_BACKENDS else soft._LINEAR_SAFE
         lib = soft._load_library()
         code = soft._DTYPE_CODES[x2.dtype]
         if m:

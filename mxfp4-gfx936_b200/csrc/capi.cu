@@ -255,8 +255,12 @@ RouteWs carve_route_ws(uint8_t* ws, int64_t num_routes, int num_experts) {
   return r;
 }
 
+// Rows of the padded routed layout, for any distribution of the routes: each
+// expert that receives a route pads its last block by at most block_m - 1
+// rows, and at most min(num_experts, num_routes) experts receive one.
 int64_t route_capacity(int64_t num_routes, int num_experts, int block_m) {
-  const int64_t padded = num_routes + static_cast<int64_t>(num_experts) * (block_m - 1);
+  const int64_t used = std::min<int64_t>(num_experts, num_routes);
+  const int64_t padded = num_routes + used * (block_m - 1);
   return (padded + block_m - 1) / block_m * block_m;
 }
 
@@ -437,19 +441,30 @@ __global__ void __launch_bounds__(256) push_rows_kernel(const uint8_t* __restric
   }
 }
 
+// The dense linear.  `w_deq` (optional) holds the weights already decoded to
+// x's dtype ([n, k], row pitch ldwd elements): the second launch of the safe
+// and decode-once paths, callable on its own (mxfp4_linear_dequantized); then
+// w_packed / w_scales are unused.
 int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw, const void* w_scales,
                 int64_t lds, const void* bias, void* out, int64_t ldo, int64_t m, int64_t n, int64_t k, int mode,
-                void* workspace, size_t workspace_bytes, void* stream, const PeerOut& peers) {
+                void* workspace, size_t workspace_bytes, void* stream, const PeerOut& peers,
+                const void* w_deq = nullptr, int64_t ldwd = 0) {
   DevInfo info;
   if (int rc = current_device_info(info)) return rc;
-  MX_CHECK(x && w_packed && w_scales && out, "null pointer");
+  MX_CHECK(x && out && (w_deq || (w_packed && w_scales)), "null pointer");
   MX_CHECK(x_dtype == MXFP4_DTYPE_BF16 || x_dtype == MXFP4_DTYPE_F16, "x must be BF16 or F16");
   MX_CHECK(mode == MXFP4_LINEAR_FUSED || mode == MXFP4_LINEAR_SAFE, "unknown linear mode");
   if (int rc = check_scales_layout(k)) return rc;
   MX_CHECK(m >= 0 && n > 0, "bad M/N");
   MX_CHECK(m < (int64_t(1) << 31) && n < (int64_t(1) << 31) && k < (int64_t(1) << 30), "dimension too large");
-  MX_CHECK(ldx >= k && ldo >= n && ldw >= k / 2 && lds >= k / 32, "leading dimension too small");
-  MX_CHECK(aligned(w_scales, 4) && lds % 4 == 0, "scales must be 4-byte aligned rows");
+  MX_CHECK(ldx >= k && ldo >= n, "leading dimension too small");
+  if (w_deq) {
+    MX_CHECK(ldwd >= k && aligned(w_deq, 16) && (ldwd * 2) % 16 == 0,
+             "dequantized weights need a 16-byte aligned base and row pitch >= k");
+  } else {
+    MX_CHECK(ldw >= k / 2 && lds >= k / 32, "leading dimension too small");
+    MX_CHECK(aligned(w_scales, 4) && lds % 4 == 0, "scales must be 4-byte aligned rows");
+  }
   if (m == 0) return MXFP4_OK;
   cudaStream_t s = as_stream(stream);
   auto push = [&](int rc) -> int {
@@ -461,12 +476,25 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
     MX_CUDA(cudaGetLastError());
     return MXFP4_OK;
   };
+  // the explicit dequant of the safe path (soft:371-373) into the workspace;
+  // afterwards `wd` / `ldwd` describe the decoded weights
+  const void* wd = w_deq;
+  auto dequant_into_workspace = [&]() -> int {
+    const size_t need = align_up(static_cast<size_t>(n) * k * 2, 256);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
+    MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
+    if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
+    wd = workspace;
+    ldwd = k;
+    return MXFP4_OK;
+  };
   const bool fp16 = x_dtype == MXFP4_DTYPE_F16;
   const CUtensorMapDataType xt = fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 
   CUtensorMap ta, tb;
   if (m <= kGemvRows && static_cast<int64_t>(kGemvRows) * k * 2 <= 200 * 1024 && aligned(x, 16) &&
-      (ldx * 2) % 16 == 0 && aligned(w_packed, 16) && ldw % 16 == 0) {
+      (ldx * 2) % 16 == 0 && (wd != nullptr || (aligned(w_packed, 16) && ldw % 16 == 0))) {
     GemvParams g{};
     g.M = static_cast<int>(m);
     g.N = static_cast<int>(n);
@@ -477,7 +505,7 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
     g.ldo = ldo;
     g.out_dtype = x_dtype;
     g.bias = bias;
-    if (mode == MXFP4_LINEAR_FUSED) {
+    if (mode == MXFP4_LINEAR_FUSED && wd == nullptr) {
       g.w = static_cast<const uint8_t*>(w_packed);
       g.ldw = ldw;
       g.w_scales = static_cast<const uint8_t*>(w_scales);
@@ -485,13 +513,10 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
       if (fp16) return push(launch_gemv<B_DECODE, true>(g, info.sms, s));
       return push(launch_gemv<B_DECODE, false>(g, info.sms, s));
     }
-    const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
-    if (workspace == nullptr || workspace_bytes < need)
-      return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
-    MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
-    if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
-    g.w = static_cast<const uint8_t*>(workspace);
-    g.ldw = k * 2;
+    if (wd == nullptr)
+      if (int rc = dequant_into_workspace()) return rc;
+    g.w = static_cast<const uint8_t*>(wd);
+    g.ldw = ldwd * 2;
     if (fp16) return push(launch_gemv<B_TMA, true>(g, info.sms, s));
     return push(launch_gemv<B_TMA, false>(g, info.sms, s));
   }
@@ -519,19 +544,16 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
     q.out_dtype = x_dtype;
     q.bias = bias;
     if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kSmBK, q.mp, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
-    if (mode == MXFP4_LINEAR_FUSED) {
+    if (mode == MXFP4_LINEAR_FUSED && wd == nullptr) {
       if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kSmBK / 2, kSmRows,
                                CU_TENSOR_MAP_SWIZZLE_NONE))
         return rc;
       if (fp16) return push(launch_small<B_DECODE, true>(ta, tb, q, s));
       return push(launch_small<B_DECODE, false>(ta, tb, q, s));
     }
-    const size_t need = mxfp4_linear_workspace_size(m, n, k, x_dtype, mode);
-    if (workspace == nullptr || workspace_bytes < need)
-      return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
-    MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
-    if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
-    if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kSmBK, kSmRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (wd == nullptr)
+      if (int rc = dequant_into_workspace()) return rc;
+    if (int rc = make_map_2d(&tb, wd, xt, 2, k, n, ldwd * 2, kSmBK, kSmRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
     if (fp16) return push(launch_small<B_TMA, true>(ta, tb, q, s));
     return push(launch_small<B_TMA, false>(ta, tb, q, s));
@@ -581,9 +603,9 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
   const int clusters = static_cast<int>(std::min<int64_t>(tiles, info.sms / 2));
 
   const size_t once_bytes = align_up(static_cast<size_t>(n) * k * 2, 256);
-  const bool decode_once = mode == MXFP4_LINEAR_FUSED && p.num_m_blocks >= kDecodeOnceRowBlocks &&
+  const bool decode_once = wd == nullptr && mode == MXFP4_LINEAR_FUSED && p.num_m_blocks >= kDecodeOnceRowBlocks &&
                            ldw == k / 2 && lds == k / 32 && workspace != nullptr && workspace_bytes >= once_bytes;
-  if (mode == MXFP4_LINEAR_FUSED && !decode_once) {
+  if (wd == nullptr && mode == MXFP4_LINEAR_FUSED && !decode_once) {
     if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kP2BK / 2,
                              p.bn / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
@@ -594,12 +616,9 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
     return fused_pair_gemm<EPI_DENSE>(fp16, ta, tb, p, clusters, s);
   }
   // safe (and fused with many row blocks): dequant of W into the workspace, then the same MMA pipeline
-  const size_t need = once_bytes;
-  if (workspace == nullptr || workspace_bytes < need)
-    return fail(MXFP4_ERR_WORKSPACE, "safe linear needs " + std::to_string(need) + " workspace bytes");
-  MX_CHECK(ldw == k / 2 && lds == k / 32, "safe mode needs contiguous packed weights and scales");
-  if (int rc = mxfp4_dequant(w_packed, w_scales, workspace, x_dtype, n, k, stream)) return rc;
-  if (int rc = make_map_2d(&tb, workspace, xt, 2, k, n, k * 2, kP2BK, p.bn / 2, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (wd == nullptr)
+    if (int rc = dequant_into_workspace()) return rc;
+  if (int rc = make_map_2d(&tb, wd, xt, 2, k, n, ldwd * 2, kP2BK, p.bn / 2, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   if (peers.n > 0) {
     if (fp16) return launch_pair<A_TMA, B_TMA, EPI_DENSE, true, 0, true>(ta, tb, p, clusters, s);
@@ -613,12 +632,22 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
 // Device-side barrier over peer-mapped flag arrays (one warp): lane j signals
 // rank j and waits for rank j's signal.  Every rank calls it the same number
 // of times; the epoch is the local call count, kept on the device so the
-// barrier works inside CUDA graphs.
+// barrier works inside CUDA graphs.  A wait longer than `limit_ns` (global
+// timer) records MXFP4_ERR_TIMEOUT and ends the kernel.
 struct PeerFlags {
   int32_t* f[kMaxPeers + 1];  // flag array [world] of each rank
 };
 
-__global__ void peer_barrier_kernel(PeerFlags flags, int rank, int world, int32_t* counter) {
+constexpr int64_t kBarrierLimitNs = 2000000000LL;  // default wait limit: 2 s
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void peer_barrier_kernel(PeerFlags flags, int rank, int world, int32_t* counter,
+                                    int64_t limit_ns = kBarrierLimitNs) {
   const int lane = threadIdx.x;
   int epoch = 0;
   if (lane == 0) {
@@ -630,16 +659,16 @@ __global__ void peer_barrier_kernel(PeerFlags flags, int rank, int world, int32_
   if (lane < world) asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flags.f[lane] + rank), "r"(epoch) : "memory");
   if (lane < world) {
     const int32_t* mine = flags.f[rank] + lane;
-    const long long t0 = clock64();
+    const uint64_t t0 = global_ns();
     while (true) {
       int32_t v;
       asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
       if (v - epoch >= 0) break;
-      if (clock64() - t0 > kWaitCycles) {
+      if (static_cast<int64_t>(global_ns() - t0) > limit_ns) {
         record_error(MXFP4_ERR_TIMEOUT);
         break;
       }
-      __nanosleep(64);
+      __nanosleep(256);
     }
   }
   __syncwarp();
@@ -655,6 +684,14 @@ int mxfp4_linear_w4a16(const void* x, int x_dtype, int64_t ldx, const void* w_pa
                        size_t workspace_bytes, void* stream) {
   return linear_impl(x, x_dtype, ldx, w_packed, ldw, w_scales, lds, bias, out, ldo, m, n, k, mode, workspace,
                      workspace_bytes, stream, PeerOut{});
+}
+
+int mxfp4_linear_dequantized(const void* x, int x_dtype, int64_t ldx, const void* w_deq, int64_t ldw,
+                             const void* bias, void* out, int64_t ldo, int64_t m, int64_t n, int64_t k,
+                             void* stream) {
+  MX_CHECK(w_deq != nullptr, "null pointer");
+  return linear_impl(x, x_dtype, ldx, nullptr, 0, nullptr, 0, bias, out, ldo, m, n, k, MXFP4_LINEAR_SAFE, nullptr, 0,
+                     stream, PeerOut{}, w_deq, ldw);
 }
 
 int mxfp4_linear_w4a16_allgather(const void* x, int x_dtype, int64_t ldx, const void* w_packed, int64_t ldw,
@@ -730,18 +767,36 @@ int mxfp4_ipc_free(void* ptr) {
   return MXFP4_OK;
 }
 
-int mxfp4_peer_barrier(int32_t* const* flags, int rank, int world, int32_t* counter, void* stream) {
+int mxfp4_peer_barrier_timed(int32_t* const* flags, int rank, int world, int32_t* counter, int64_t timeout_us,
+                             void* stream) {
   DevInfo info;
   if (int rc = current_device_info(info)) return rc;
   MX_CHECK(world >= 1 && world <= kMaxPeers + 1 && rank >= 0 && rank < world, "bad rank/world");
   MX_CHECK(flags != nullptr && counter != nullptr, "null pointer");
+  MX_CHECK(timeout_us >= 0 && timeout_us <= int64_t(60) * 1000 * 1000, "timeout_us must be in [0, 60 s]");
   PeerFlags f{};
   for (int j = 0; j < world; ++j) {
     MX_CHECK(flags[j] != nullptr && aligned(flags[j], 4), "flag arrays must be non-null and 4-byte aligned");
     f.f[j] = flags[j];
   }
-  peer_barrier_kernel<<<1, 32, 0, as_stream(stream)>>>(f, rank, world, counter);
+  const int64_t limit_ns = timeout_us > 0 ? timeout_us * 1000 : kBarrierLimitNs;
+  peer_barrier_kernel<<<1, 32, 0, as_stream(stream)>>>(f, rank, world, counter, limit_ns);
   MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+int mxfp4_peer_barrier(int32_t* const* flags, int rank, int world, int32_t* counter, void* stream) {
+  return mxfp4_peer_barrier_timed(flags, rank, world, counter, 0, stream);
+}
+
+int mxfp4_peer_barrier_reset(int32_t* local_flags, int world, int32_t* counter, void* stream) {
+  DevInfo info;
+  if (int rc = current_device_info(info)) return rc;
+  MX_CHECK(world >= 1 && world <= kMaxPeers + 1, "bad world");
+  MX_CHECK(local_flags != nullptr && counter != nullptr, "null pointer");
+  cudaStream_t s = as_stream(stream);
+  MX_CUDA(cudaMemsetAsync(local_flags, 0, sizeof(int32_t) * world, s));
+  MX_CUDA(cudaMemsetAsync(counter, 0, sizeof(int32_t), s));
   return MXFP4_OK;
 }
 
@@ -795,20 +850,49 @@ int mxfp4_moe_route(const void* topk_ids, int ids_dtype, int64_t num_tokens, int
                    as_stream(stream));
 }
 
-// Workspace of the routed op: routing arrays, routing scratch, converted A.
+}  // extern "C"
+
+namespace {
+
+// Tensor-core operand type of the routed op and how many BF16 parts each
+// activation is split into.  C's dtype is the matmul dtype (soft:405):
+//  - C BF16 / F16: A rounded to C's dtype (soft:475), one part;
+//  - C F32: the products of an FP32 matmul.  BF16 and dequantised MXFP4
+//    activations are exact in BF16 (one part); F16 activations are the exact
+//    sum of two BF16 parts and F32 activations of three, each part multiplied
+//    by the exactly decoded BF16 weights with FP32 accumulation.
+struct MoeCompute {
+  int dtype;  // BF16 or F16
+  int parts;  // 1, 2 or 3
+};
+
+MoeCompute moe_compute(int a_dtype, int c_dtype) {
+  if (c_dtype != MXFP4_DTYPE_F32) return {c_dtype, 1};
+  if (a_dtype == MXFP4_DTYPE_F32) return {MXFP4_DTYPE_BF16, 3};
+  if (a_dtype == MXFP4_DTYPE_F16) return {MXFP4_DTYPE_BF16, 2};
+  return {MXFP4_DTYPE_BF16, 1};
+}
+
+}  // namespace
+
+extern "C" {
+
+// Workspace of the routed op: routing arrays, routing scratch, converted A,
+// activations in routed order.
 size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t n,
                                       int64_t k, int a_dtype, int c_dtype) {
   (void)n;
   const int64_t routes = num_tokens * top_k;
   const int64_t cap = route_capacity(routes, num_experts, kP2BM);
+  const MoeCompute mc = moe_compute(a_dtype, c_dtype);
+  const int64_t ka = k * mc.parts;  // columns of the converted activations
   size_t b = 0;
   b += align_up(sizeof(int32_t) * cap, 256);
   b += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
   b += 256;  // num_post_padded
   b += route_ws_bytes(routes, num_experts);
-  const int cdt = c_dtype == MXFP4_DTYPE_F32 ? a_dtype : c_dtype;
-  if (a_dtype != cdt || a_dtype == MXFP4_DTYPE_U8) b += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
-  b += align_up(static_cast<size_t>(cap) * k * 2, 256);  // activations in routed order
+  if (a_dtype != mc.dtype || mc.parts > 1) b += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
+  b += align_up(static_cast<size_t>(cap) * ka * 2, 256);  // activations in routed order
   return b;
 }
 
@@ -834,13 +918,10 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   MX_CHECK(num_tokens >= 0 && top_k > 0 && num_experts > 0 && num_experts <= kMaxExperts && n > 0,
            "bad sizes");
   MX_CHECK(num_tokens * top_k < (int64_t(1) << 31) && n < (int64_t(1) << 31), "dimension too large");
-  // the compute dtype of the MMA: C's dtype, or A's 16-bit dtype when C is F32
-  int cdt = c_dtype;
-  if (c_dtype == MXFP4_DTYPE_F32) {
-    if (a_dtype == MXFP4_DTYPE_F32)
-      return fail(MXFP4_ERR_UNSUPPORTED, "F32 activations with an F32 output are not supported by the B200 backend");
-    cdt = a_dtype == MXFP4_DTYPE_U8 ? MXFP4_DTYPE_BF16 : a_dtype;
-  }
+  MX_CHECK(k < (int64_t(1) << 30), "dimension too large");
+  const MoeCompute mc = moe_compute(a_dtype, c_dtype);
+  const int cdt = mc.dtype;
+  const int64_t ka = k * mc.parts;  // K of the converted activations (k_rep parts)
   const size_t need = mxfp4_fused_moe_workspace_size(num_tokens, top_k, num_experts, n, k, a_dtype, c_dtype);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(MXFP4_ERR_WORKSPACE, "fused MoE needs " + std::to_string(need) + " workspace bytes");
@@ -865,6 +946,12 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   if (a_dtype == MXFP4_DTYPE_U8) {
     if (int rc = mxfp4_dequant(A, a_mx_scale, ws, cdt, num_tokens, k, stream)) return rc;
     a_eff = ws;
+  } else if (mc.parts > 1) {
+    const int64_t cnt = num_tokens * k;
+    const int grid = static_cast<int>(std::min<int64_t>((cnt + 255) / 256, int64_t(info.sms) * 8));
+    split_bf16_kernel<<<grid, 256, 0, s>>>(A, a_dtype, num_tokens, k, mc.parts, reinterpret_cast<__nv_bfloat16*>(ws));
+    MX_CUDA(cudaGetLastError());
+    a_eff = ws;
   } else if (a_dtype != cdt) {
     const int64_t cnt = num_tokens * k;
     const int grid = static_cast<int>(std::min<int64_t>((cnt + 255) / 256, int64_t(info.sms) * 8));
@@ -876,25 +963,26 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
                          route_ws, s))
     return rc;
   MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
-  if (a_eff != A) ws += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
+  if (a_eff != A) ws += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
   void* a_routed = ws;
-  if (int rc = run_gather(a_eff, k, sorted_ids, post, routes, top_k, a_routed, cap, info.sms, s)) return rc;
+  if (int rc = run_gather(a_eff, ka, sorted_ids, post, routes, top_k, a_routed, cap, info.sms, s)) return rc;
 
   CUtensorMap ta, tb;
   const CUtensorMapDataType at = cdt == MXFP4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  if (int rc = make_map_2d(&ta, a_routed, at, 2, k, cap, k * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (int rc = make_map_2d(&ta, a_routed, at, 2, ka, cap, ka * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, static_cast<uint64_t>(num_experts) * n,
                            k / 2, kP2BK / 2, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
   PairParams p{};
   p.N = static_cast<int>(n);
-  p.K = static_cast<int>(k);
+  p.K = static_cast<int>(ka);
+  p.k_rep = mc.parts;
   p.bn = 256;
   p.num_m_blocks = static_cast<int>(cap / kP2BM);
   p.num_n_blocks = static_cast<int>((n + p.bn - 1) / p.bn);
   p.a_ptr = static_cast<const uint8_t*>(a_eff);
-  p.lda = k;
+  p.lda = ka;
   p.w_scales = static_cast<const uint8_t*>(B_mx_scale);
   p.lds = k / 32;
   p.w_rows_per_expert = n;
@@ -920,15 +1008,28 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
 // g_noalloc_scratch array instead of a caller workspace: no cudaMalloc, no
 // cudaFree, no allocating library call.  Requests whose scratch would exceed
 // kNoAllocScratchBytes are rejected.  All calls share the array, so calls that
-// overlap on the GPU race; nothing in it needs to start at zero (every byte a
-// call reads was written earlier in the same call).
+// overlap on the GPU race.  Nothing in it needs to start at zero: every byte
+// that decides a result is written earlier in the same call (routing arrays,
+// converted and routed activation rows); the padding rows of the routed copy
+// keep whatever an earlier call left there, and the GEMM reads them but
+// discards their results.
 int mxfp4_fused_moe_noalloc(const void* A, int a_dtype, const void* a_mx_scale, const void* B,
                             const void* B_mx_scale, const float* a_scale, const float* b_scale,
                             const void* topk_weights, int w_dtype, const void* topk_ids, int ids_dtype,
                             void* C, int c_dtype, int64_t num_tokens, int top_k, int num_experts,
                             int64_t n, int64_t k, int mul_routed_weight, void* stream) {
-  if (num_tokens < 0 || top_k <= 0 || num_experts <= 0 || num_experts > kMaxExperts)
-    return fail(MXFP4_ERR_INVALID_ARGUMENT, "bad sizes");
+  // the sizes and dtypes the workspace size depends on are checked first, so a
+  // bad argument is reported as one and not as a scratch overflow
+  MX_CHECK(num_tokens >= 0 && top_k > 0 && num_experts > 0 && num_experts <= kMaxExperts && n > 0,
+           "bad sizes");
+  MX_CHECK(num_tokens * top_k < (int64_t(1) << 31) && n < (int64_t(1) << 31), "dimension too large");
+  if (int rc = check_scales_layout(k)) return rc;
+  MX_CHECK(k < (int64_t(1) << 30), "dimension too large");
+  MX_CHECK(c_dtype == MXFP4_DTYPE_F32 || c_dtype == MXFP4_DTYPE_BF16 || c_dtype == MXFP4_DTYPE_F16,
+           "C must be F32, BF16 or F16");
+  MX_CHECK(a_dtype == MXFP4_DTYPE_U8 || a_dtype == MXFP4_DTYPE_BF16 || a_dtype == MXFP4_DTYPE_F16 ||
+               a_dtype == MXFP4_DTYPE_F32,
+           "A must be U8 (packed MXFP4), BF16, F16 or F32");
   const size_t need = mxfp4_fused_moe_workspace_size(num_tokens, top_k, num_experts, n, k, a_dtype, c_dtype);
   if (need > kNoAllocScratchBytes)
     return fail(MXFP4_ERR_WORKSPACE, "mxfp4_fused_moe_noalloc needs " + std::to_string(need) +

@@ -72,6 +72,36 @@ __global__ void __launch_bounds__(256) cast_kernel(const void* __restrict__ src,
   }
 }
 
+// Exact split of F16 / F32 activations into `parts` BF16 values whose sum is
+// the input: hi = bf16(a), mid = bf16(a - hi), lo = bf16(a - hi - mid).  An F16
+// value (11 significant bits) is hi + mid exactly; an F32 value (24 bits) is
+// hi + mid + lo exactly unless its last bits lie below the BF16 subnormal
+// range (|a| < 2^-109).  Each part times an exactly decoded BF16 weight is an
+// exact FP32 product, so the FP32-output routed op computes the products of an
+// FP32 matmul on the BF16 tensor cores.  Part r of row i lands in columns
+// [r*k, (r+1)*k) of out row i (row stride parts*k); infinities and NaNs go
+// whole into the first part.
+__global__ void __launch_bounds__(256) split_bf16_kernel(const void* __restrict__ src, int src_dtype,
+                                                         int64_t rows, int64_t k, int parts,
+                                                         __nv_bfloat16* __restrict__ dst) {
+  const int64_t n = rows * k;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float a = src_dtype == MXFP4_DTYPE_F32 ? static_cast<const float*>(src)[i]
+                                                 : __half2float(static_cast<const __half*>(src)[i]);
+    const int64_t r = i / k, c = i % k;
+    __nv_bfloat16* row = dst + r * parts * k + c;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(a);
+    float rem = isfinite(a) ? a - __bfloat162float(hi) : 0.0f;
+    row[0] = hi;
+    for (int q = 1; q < parts; ++q) {
+      const __nv_bfloat16 part = __float2bfloat16_rn(rem);
+      rem -= __bfloat162float(part);
+      row[static_cast<int64_t>(q) * k] = part;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // K4 routing, three passes over the routes (stable counting sort):
 //   pass 1 (route_count): each CTA takes a contiguous chunk of routes, ranks

@@ -145,6 +145,10 @@ struct PairParams {
   int64_t lds;
   int64_t w_rows_per_expert;       // N (plain) or 2*inter (GLU)
   int glu_inter;
+  // K of A is k_rep copies of the weights' K (0 or 1: one): A row =
+  // [part 0 | part 1 | ...], every part multiplied by the same weights, so
+  // the weight stages (packed tile and scale words) repeat every K/k_rep
+  int k_rep;
   // routing
   const int32_t* sorted_ids;
   const int32_t* block_expert;
@@ -431,6 +435,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int KT = p.K / kP2BK;
+  const int KTw = p.k_rep > 1 ? KT / p.k_rep : KT;  // weight stages per pass over the weights' K
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
   const int half_rows = p.bn / 2;
@@ -513,7 +518,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
           armed_par = (armed_par & ~(1u << s)) | (ph << s);
           if (AMODE == A_TMA) tma_load_2d(smem + Cfg::kOffA + s * kP2ABytes, &tmap_a, &full[s], kt * kP2BK, arow);
           if (BMODE == B_DECODE)
-            tma_load_2d_hint(smem + Cfg::kOffP + s * kP2PBytes, &tmap_b, &full[s], kt * (kP2BK / 2), brow, pol_w);
+            tma_load_2d_hint(smem + Cfg::kOffP + s * kP2PBytes, &tmap_b, &full[s], (kt % KTw) * (kP2BK / 2), brow,
+                             pol_w);
           else
             tma_load_2d_hint(smem + Cfg::kOffB + s * kP2BBytes, &tmap_b, &full[s], kt * kP2BK, brow, pol_w);
         }
@@ -651,17 +657,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
         const int64_t grow = pair_weight_row<EPI>(p, c, rank, r, valid);
         valid = valid && row_live;
         const uint8_t* srow = p.w_scales + (valid ? grow * p.lds : 0);
-        // one 32-bit scale word covers two 64-K stages; keep two words in flight
-        const int nwords = KT / 2;
+        // one 32-bit scale word covers two 64-K stages; keep two words in flight.
+        // The word sequence repeats every nwords words when A holds k_rep parts
+        // (KTw is even: K is a multiple of 128).
+        const int nwords = KTw / 2;
+        const int nwords_all = KT / 2;
         uint32_t w0 = valid ? ldg_nc_u32(srow) : 0x7F7F7F7Fu;
-        uint32_t w1 = (valid && nwords > 1) ? ldg_nc_u32(srow + 4) : 0x7F7F7F7Fu;
+        uint32_t w1 = (valid && nwords_all > 1) ? ldg_nc_u32(srow + 4 * (1 % nwords)) : 0x7F7F7F7Fu;
         uint32_t cur = 0;
         for (int kt = 0; kt < KT; ++kt, ++it) {
           if ((kt & 1) == 0) {
             cur = w0;
             w0 = w1;
             const int nw = (kt >> 1) + 2;
-            if (valid && nw < nwords) w1 = ldg_nc_u32(srow + 4 * nw);
+            if (valid && nw < nwords_all) w1 = ldg_nc_u32(srow + 4 * (nw % nwords));
           }
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;

@@ -19,13 +19,25 @@ Backend selection is explicit, as in soft:45-49.  ``MXFP4_GFX936_BACKEND``
 * ``safe`` (default): explicit dequantisation of the weight into a workspace
   (the ``dequant_mxfp4`` kernel), then the tcgen05 GEMM on that BF16/FP16
   weight -- the structure of soft:371-373;
-* ``fused`` (``triton`` is accepted as the reference adapter's name for the
-  fused path, vllm:34-36): the weight is decoded inside the GEMM producer, the
-  B200 counterpart of soft:176-274.  There is no shape guard: both modes feed
-  the same MMA sequence, so their results are identical bit for bit.
+* ``triton`` (the reference's name, also what the vLLM adapter writes,
+  vllm:34-36) and ``fused`` (the same mode under its B200 name): the weight is
+  decoded inside the GEMM producer, the B200 counterpart of soft:176-274.
+  There is no shape guard: both modes feed the same MMA sequence, so their
+  results are identical bit for bit.
 
 The routed-MoE op has one native path (device routing + grouped GEMM) for
-both values.  Any other value raises ``ValueError``.
+every value.  With ``triton`` it also keeps the reference Triton path's input
+contract (soft:409-430: unpacked activations and valid padded routing
+metadata, else ``RuntimeError``); ``fused`` accepts packed activations and
+empty metadata as well.  Any other value raises ``ValueError``.
+
+The reference module's helpers keep their names and contracts (soft:34-62):
+``_has_compatible_triton_compiler`` answers whether the prebuilt sm_100a
+library loads on an sm_100 device (this backend's counterpart of the gfx936
+compiler probe), ``_require_triton_compiler`` raises ``RuntimeError`` when it
+does not, and ``_is_validated_triton_linear_shape`` keeps the reference's
+M >= 370 and N >= 2048 rule.  The B200 fused path covers every shape, so the
+operator does not consult that rule.
 """
 
 from __future__ import annotations
@@ -56,8 +68,8 @@ _MXFP4_E2M1_VALUES = (
     -6.0,
 )
 
-_BACKENDS = ("safe", "fused")
-_BACKEND_ALIASES = {"triton": "fused"}
+_BACKENDS = ("safe", "triton", "fused")
+_FUSED_BACKENDS = ("triton", "fused")
 
 # C ABI constants (include/mxfp4_b200.h)
 _OK = 0
@@ -100,6 +112,7 @@ _SIGNATURES = {
         _INT,
         [_VP, _INT, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64, _INT, _VP, _SZ, _VP],
     ),
+    "mxfp4_linear_dequantized": (_INT, [_VP, _INT, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64, _VP]),
     "mxfp4_quantize": (_INT, [_VP, _INT, _I64, _I64, _I64, _VP, _VP, _VP]),
     "mxfp4_moe_router": (_INT, [_VP, _INT, _I64, _INT, _INT, _INT, _VP, _VP, _VP]),
     "mxfp4_gemm_w4a4_workspace_size": (_SZ, [_I64, _I64, _I64]),
@@ -129,6 +142,8 @@ _SIGNATURES = {
          _I64, _I64, _INT, _VP, _SZ, _VP],
     ),
     "mxfp4_peer_barrier": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT, _INT, _VP, _VP]),
+    "mxfp4_peer_barrier_timed": (_INT, [ctypes.POINTER(ctypes.c_void_p), _INT, _INT, _VP, _I64, _VP]),
+    "mxfp4_peer_barrier_reset": (_INT, [_VP, _INT, _VP, _VP]),
     "mxfp4_ipc_alloc": (_INT, [_SZ, ctypes.POINTER(ctypes.c_void_p), _VP]),
     "mxfp4_ipc_open": (_INT, [_VP, ctypes.POINTER(ctypes.c_void_p)]),
     "mxfp4_ipc_close": (_INT, [_VP]),
@@ -180,12 +195,38 @@ def _has_compatible_native_library() -> bool:
     return bool(lib.mxfp4_device_supported(torch.cuda.current_device()))
 
 
+@functools.lru_cache(maxsize=1)
+def _has_compatible_triton_compiler() -> bool:
+    """soft:34-43 under the same name.  The fused backend's kernels come
+    prebuilt for sm_100a, so its "compiler" is libmxfp4_b200.so itself: true
+    when that library loads and the current CUDA device is sm_100."""
+    return _has_compatible_native_library()
+
+
 def _backend() -> str:
+    """soft:45-49: ``MXFP4_GFX936_BACKEND`` read on every call, ``safe`` by
+    default; ``triton`` and ``fused`` both select the fused-decode GEMM."""
     backend = os.getenv("MXFP4_GFX936_BACKEND", "safe")
-    backend = _BACKEND_ALIASES.get(backend, backend)
     if backend not in _BACKENDS:
-        raise ValueError(f"unknown B200 MXFP4 backend: {backend}")
+        raise ValueError(f"unknown gfx936 MXFP4 backend: {backend} (B200 backend: safe, triton or fused)")
     return backend
+
+
+def _require_triton_compiler() -> None:
+    """soft:52-57: the fused backend fails loud when its kernels cannot run."""
+    if not _has_compatible_triton_compiler():
+        raise RuntimeError(
+            "MXFP4_GFX936_BACKEND=triton requires a compatible compiler; on B200 that is the prebuilt "
+            "sm_100a library libmxfp4_b200.so on an sm_100 device (set MXFP4_B200_LIBRARY explicitly; "
+            "TRITON_HIP_CLANG_PATH is not used by this backend)"
+        )
+
+
+def _is_validated_triton_linear_shape(m: int, n: int) -> bool:
+    """soft:60-62: the shape range the reference validated its Triton linear
+    on (M >= 370 and N >= 2048).  Kept for callers and tests that read it; the
+    B200 fused linear covers every shape with the same bits as ``safe``."""
+    return m >= 370 and n >= 2048
 
 
 def _require_native_library() -> None:
@@ -307,6 +348,8 @@ def linear_mxfp4_soft(
         raise ValueError("one E8M0 scale is required for every 32 MXFP4 values")
 
     backend = _backend()
+    if backend in _FUSED_BACKENDS:
+        _require_triton_compiler()
     device = _require_cuda(x, packed, block_scales, bias)
     input_shape = x.shape
     n = packed.shape[0]
@@ -317,7 +360,7 @@ def linear_mxfp4_soft(
     b = _dense(bias) if fused_bias else None
     w = _dense(packed)
     s = _dense(block_scales)
-    mode = _LINEAR_FUSED if backend == "fused" else _LINEAR_SAFE
+    mode = _LINEAR_FUSED if backend in _FUSED_BACKENDS else _LINEAR_SAFE
     lib = _load_library()
     if m:
         code = _DTYPE_CODES[x.dtype]
@@ -330,6 +373,36 @@ def linear_mxfp4_soft(
     if bias is not None and not fused_bias:
         output = output + bias
     return output.reshape(*input_shape[:-1], n)
+
+
+def linear_dequantized(x: torch.Tensor, w_deq: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ w_deq.T`` (+ ``bias``) for weights already decoded by
+    ``dequant_mxfp4`` into x's dtype: the matmul half of the safe path
+    (soft:372-375) on the same kernels as ``linear_mxfp4_soft``, so
+    ``linear_dequantized(x, dequant_mxfp4(W, S, x.dtype))`` has the bits of
+    ``linear_mxfp4_soft(x, W, S)``.  K must be a multiple of 128."""
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError(f"x must be fp16 or bf16, got {x.dtype}")
+    if w_deq.dtype != x.dtype or w_deq.ndim != 2:
+        raise TypeError("w_deq must be a 2-D tensor of x's dtype")
+    k = w_deq.shape[1]
+    if x.shape[-1] != k or k % 128:
+        raise ValueError(f"input K {x.shape[-1]} must match weight K {k}, a multiple of 128")
+    device = _require_cuda(x, w_deq, bias)
+    n = w_deq.shape[0]
+    x_2d = _dense(x.reshape(-1, k))
+    m = x_2d.shape[0]
+    out = torch.empty((m, n), dtype=x.dtype, device=device)
+    fused_bias = bias is not None and bias.dtype == x.dtype and tuple(bias.shape) == (n,)
+    b = _dense(bias) if fused_bias else None
+    w = _dense(w_deq)
+    if m:
+        with torch.cuda.device(device):
+            _check(_load_library().mxfp4_linear_dequantized(
+                _ptr(x_2d), _DTYPE_CODES[x.dtype], k, _ptr(w), k, _ptr(b), _ptr(out), n, m, n, k, _stream(device)))
+    if bias is not None and not fused_bias:
+        out = out + bias
+    return out.reshape(*x.shape[:-1], n)
 
 
 # ---------------------------------------------------------------------------
@@ -359,21 +432,45 @@ def fused_moe_mxfp4_soft(
     ``C[t, j, :] = A[t] . deq(B[e])^T * A_scale * B_scale[e]`` (times the
     route weight when ``mul_routed_weight``), with C's dtype as the compute
     dtype and the rounding points of soft:487-494, for e = topk_ids[t, j].
+    With an FP32 ``C`` the products and sums are those of an FP32 matmul
+    (soft:405, 466-494): activations are split exactly into BF16 parts and
+    every part meets the exactly decoded BF16 weights with FP32 accumulation.
     Routes whose expert id lies outside ``[0, B.shape[0])`` leave zeros.  The
-    padded routing metadata of the Triton path is accepted and ignored: the
-    kernel derives its own 128-row blocks from ``topk_ids`` on the device.
+    padded routing metadata of the Triton path is validated like the
+    reference's (backend ``triton``) and then ignored: the kernel derives its
+    own route blocks from ``topk_ids`` on the device.
     """
     if swizzle_mx_a or swizzle_mx_b:
-        raise NotImplementedError("the B200 MXFP4 backend does not support swizzled scales")
+        raise NotImplementedError(
+            "the gfx936 software fallback does not support swizzled scales; the B200 backend keeps that contract")
     if topk_ids.shape != topk_weights.shape or topk_ids.shape[1] != top_k:
         raise ValueError("top-k ids and weights must have matching (M, top_k) shapes")
     if B.dtype != torch.uint8 or B_mx_scale is None:
-        raise TypeError("the B200 MXFP4 backend requires packed MXFP4 weights")
+        raise TypeError("the gfx936 software fallback requires packed MXFP4 weights (B200 backend)")
 
     matmul_dtype = C.dtype
     if matmul_dtype not in (torch.float16, torch.bfloat16, torch.float32):
-        raise TypeError(f"unsupported B200 MXFP4 compute dtype: {matmul_dtype}")
-    _backend()
+        raise TypeError(f"unsupported software fallback compute dtype: {matmul_dtype}")
+    backend = _backend()
+    if backend == "triton":
+        # the reference Triton path's input contract (soft:409-430)
+        _require_triton_compiler()
+        routing_ready = (
+            A.dtype != torch.uint8
+            and sorted_token_ids.numel() > 0
+            and expert_ids.numel() > 0
+            and num_tokens_post_padded.numel() == 1
+            and B.shape[-1] * 2 % 128 == 0
+            and sorted_token_ids.numel() % expert_ids.numel() == 0
+        )
+        if not routing_ready:
+            raise RuntimeError(
+                "the experimental Triton MoE backend requires unpacked "
+                "activations and valid padded routing metadata"
+            )
+        block_m = sorted_token_ids.numel() // expert_ids.numel()
+        if block_m not in (16, 32, 64, 128):
+            raise RuntimeError(f"unsupported Triton routing block size: {block_m}")
     del sorted_token_ids, expert_ids, num_tokens_post_padded
 
     if A.dtype == torch.uint8:

@@ -123,18 +123,50 @@ def _check(lib, rc: int) -> None:
         raise RuntimeError(f"libmxfp4_b200 error {rc}: {lib.mxfp4_last_error().decode(errors='replace')}")
 
 
-class PeerBarrier:
-    """Device-side barrier of the ranks of ``group`` (collective constructor)."""
+def reset_protocol(quiesce, reset_local, host_barrier) -> None:
+    """Collective reset of a device barrier whose epochs may disagree (after a
+    bounded wait recorded MXFP4_ERR_TIMEOUT): every rank first waits until its
+    own barrier kernels have finished (``quiesce``), a host barrier makes sure
+    no rank's kernel can still store into a peer's flags, each rank zeroes its
+    own flags and counter (``reset_local``, completed by a second ``quiesce``),
+    and a second host barrier keeps every rank from signalling again before
+    all have reset."""
+    quiesce()
+    host_barrier()
+    reset_local()
+    quiesce()
+    host_barrier()
 
-    def __init__(self, group=None):
+
+class PeerBarrier:
+    """Device-side barrier of the ranks of ``group`` (collective constructor).
+
+    ``timeout_us`` bounds every wait (0: the library default of 2 s); a wait
+    that runs out records MXFP4_ERR_TIMEOUT in the device status word.  After
+    that, call ``reset()`` on every rank before using the barrier again."""
+
+    def __init__(self, group=None, timeout_us: int = 0):
+        self.group = group
         self.flags = PeerBuffers((8,), torch.int32, group)  # zero-filled
         self.counter = torch.zeros(1, dtype=torch.int32, device=self.flags.local.device)
         self.rank, self.world = self.flags.rank, self.flags.world
+        self.timeout_us = int(timeout_us)
         self._flag_ptrs = pointer_array(self.flags.ptrs)
         self._lib = _soft()._load_library()
 
     def __call__(self, stream: torch.cuda.Stream | None = None) -> None:
         s = stream if stream is not None else torch.cuda.current_stream()
-        rc = self._lib.mxfp4_peer_barrier(ctypes.cast(self._flag_ptrs, _VPP), self.rank, self.world,
-                                          self.counter.data_ptr(), s.cuda_stream)
+        rc = self._lib.mxfp4_peer_barrier_timed(ctypes.cast(self._flag_ptrs, _VPP), self.rank, self.world,
+                                                self.counter.data_ptr(), self.timeout_us, s.cuda_stream)
         _check(self._lib, rc)
+
+    def reset(self) -> None:
+        """Collective: zero every rank's flags and counter (``reset_protocol``)."""
+        device = self.counter.device
+
+        def reset_local():
+            _check(self._lib, self._lib.mxfp4_peer_barrier_reset(
+                ctypes.c_void_p(self.flags.ptrs[self.rank]), self.world, ctypes.c_void_p(self.counter.data_ptr()),
+                torch.cuda.current_stream(device).cuda_stream))
+
+        reset_protocol(lambda: torch.cuda.synchronize(device), reset_local, lambda: dist.barrier(group=self.group))

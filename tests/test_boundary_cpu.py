@@ -53,7 +53,7 @@ def test_safe_backend_is_default(monkeypatch):
     assert soft._backend() == "safe"
 
 
-@pytest.mark.parametrize("value,expected", [("safe", "safe"), ("fused", "fused"), ("triton", "fused")])
+@pytest.mark.parametrize("value,expected", [("safe", "safe"), ("fused", "fused"), ("triton", "triton")])
 def test_explicit_backend_values(monkeypatch, value, expected):
     monkeypatch.setenv("MXFP4_GFX936_BACKEND", value)
     assert soft._backend() == expected
@@ -61,7 +61,7 @@ def test_explicit_backend_values(monkeypatch, value, expected):
 
 def test_unknown_backend_fails_loud(monkeypatch):
     monkeypatch.setenv("MXFP4_GFX936_BACKEND", "unknown")
-    with pytest.raises(ValueError, match="unknown B200 MXFP4 backend"):
+    with pytest.raises(ValueError, match="unknown gfx936 MXFP4 backend"):
         soft._backend()
 
 
@@ -150,7 +150,7 @@ def test_moe_validation_matches_reference():
 
 def test_unknown_backend_rejected_by_ops(monkeypatch):
     monkeypatch.setenv("MXFP4_GFX936_BACKEND", "bogus")
-    with pytest.raises(ValueError, match="unknown B200 MXFP4 backend"):
+    with pytest.raises(ValueError, match="unknown gfx936 MXFP4 backend"):
         soft.linear_mxfp4_soft(torch.zeros(2, 128, dtype=torch.bfloat16),
                                torch.zeros(64, 64, dtype=torch.uint8), torch.zeros(64, 4, dtype=torch.uint8))
 
@@ -195,3 +195,36 @@ def test_routing_and_ep_capacities_hold_every_layout():
             assert _padded_rows(dist_, 256) <= cap
     assert lib.mxfp4_ep_moe_recv_capacity(10, 2, 10, 4) == 0  # experts must divide over the ranks
     assert lib.mxfp4_ep_moe_recv_capacity(-1, 2, 8, 4) == 0
+
+
+def test_noalloc_checks_arguments_before_sizing_its_scratch():
+    # a bad K or dtype is an invalid argument, not a scratch overflow; both
+    # answers come from host validation before any device call
+    lib = soft._load_library()
+    null = ctypes.c_void_p(0)
+    BF16, F32, I64 = 1, 0, 5
+
+    def call(t, k, a_dtype=BF16, c_dtype=BF16, n=256):
+        return lib.mxfp4_fused_moe_noalloc(null, a_dtype, null, null, null, null, null, null, F32, null, I64, null,
+                                           c_dtype, t, 2, 8, n, k, 0, null)
+
+    assert call(8, -128) == 1
+    assert call(8, 100) == 1
+    assert call(8, 128, a_dtype=7) == 1
+    assert call(8, 128, c_dtype=3) == 1
+    assert call(8, 128, n=0) == 1
+    assert call(1 << 20, 128) == 5  # a valid request whose scratch exceeds the static array
+
+
+def test_probe_library_exports_its_header():
+    # the benchmark's tensor-core rate probe is a separate library with its own header
+    text = (ROOT / "include" / "mxfp4_b200_probe.h").read_text()
+    names = re.findall(r"^\s*int\s+(mxfp4_\w+)\s*\(", text, re.M)
+    assert names == ["mxfp4_probe_mma_rate"]
+    lib = ctypes.CDLL(str(PKG / "libmxfp4_b200_probe.so"))
+    assert all(hasattr(lib, n) for n in names)
+    # argument checks answer before any device call
+    fn = lib.mxfp4_probe_mma_rate
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    assert fn(7, 10, None, None, None) == 1

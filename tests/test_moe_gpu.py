@@ -103,6 +103,33 @@ def test_moe_op_dtypes_and_dropped_routes(c_dtype, a_dtype, m, n, k, e, top_k):
     assert ok, (err, bound, rel)
 
 
+@pytest.mark.parametrize("a_dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("lo,hi", [(118, 131), (140, 151), (100, 112)])
+def test_moe_op_fp32_output_at_fp32_precision(a_dtype, lo, hi):
+    # C = F32 makes the matmul FP32 (soft:405, 466-494): F16 weights would
+    # overflow from scale code 143 on and flush small scales, BF16-rounded F32
+    # activations would lose 16 bits; the split-activation path keeps both exact
+    m, n, k, e, top_k = 45, 192, 384, 5, 2
+    g = torch.Generator().manual_seed(lo + m)
+    a = (torch.randn(m, k, generator=g) * 3).to(a_dtype)
+    b = torch.randint(0, 256, (e, n, k // 2), generator=g, dtype=torch.uint8)
+    bmx = torch.randint(lo, hi, (e, n, k // 32), generator=g, dtype=torch.uint8)
+    ids = torch.randint(0, e, (m, top_k), generator=g, dtype=torch.int64)
+    tw = torch.rand(m, top_k, generator=g)
+    a_scale, b_scale = torch.tensor([0.75]), torch.linspace(0.5, 1.25, e)
+    c = torch.full((m, top_k, n), 7.0, dtype=torch.float32, device="cuda")
+    soft.fused_moe_mxfp4_soft(a.cuda(), b.cuda(), c, a_scale.cuda(), b_scale.cuda(), None, bmx.cuda(), tw.cuda(),
+                              ids.cuda(), torch.empty(0), torch.empty(0), torch.empty(0), True, top_k, False, False)
+    ref = O.moe_op(_np(a), "fp32", None, b.numpy(), bmx.numpy(), a_scale.numpy(), b_scale.numpy(), tw.numpy(),
+                   ids.numpy(), True, "fp32")
+    got = _np(c)
+    assert np.isfinite(got).all() and np.isfinite(ref).all()
+    ok, err, bound, rel = O.check_close(got, ref)
+    assert ok, (err, bound, rel)
+    # FP32 products and FP32 sums: far inside the BF16-scale gate
+    assert rel < 1e-5, rel
+
+
 # --------------------------------------------------------------------------- MoE layer
 def test_moe_layer_matches_reference_golden():
     g = golden("moe_layer")

@@ -198,3 +198,46 @@ def test_column_parallel_multicast_policy_gloo():
         assert out["eight"] == (["symm-try", "symm-try"], "FakeSymm"), out
         assert out["forced"] == "raised", out
         assert out["fallback"] == "FakeIpc", out
+
+
+def _reset_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    pm = load_by_path("mxfp4_peer_memory", PKG / "peer_memory.py")
+    import time
+    events = []
+
+    def quiesce():
+        events.append(("quiesce", time.monotonic()))
+
+    def reset_local():
+        if rank == 1:
+            time.sleep(0.3)  # a slow rank: nobody may resume before it has reset
+        events.append(("reset", time.monotonic()))
+
+    pm.reset_protocol(quiesce, reset_local, dist.barrier)
+    events.append(("resume", time.monotonic()))
+    q.put((rank, events))
+    dist.destroy_process_group()
+
+
+def test_barrier_reset_protocol_orders_ranks_gloo():
+    # after a timed-out device barrier every rank resets its own flags; no rank
+    # may reset while a peer's barrier kernel could still run, and no rank may
+    # signal again before every rank has reset
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_reset_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    first_quiesce = [got[r][0] for r in range(2)]
+    assert all(e[0] == "quiesce" for e in first_quiesce)
+    resets = [next(t for name, t in got[r] if name == "reset") for r in range(2)]
+    resumes = [next(t for name, t in got[r] if name == "resume") for r in range(2)]
+    assert max(e[1] for e in first_quiesce) <= min(resets)
+    assert max(resets) <= min(resumes)
