@@ -464,6 +464,90 @@ def bench_w4a4(soft, steps, warmup, device):
     return ms
 
 
+STACK_PREFILL = (8, 2048)        # sequences x tokens
+STACK_DECODE_BATCHES = (1, 8, 64, 256)
+STACK_DECODE_CTX = 2048          # decode continues 2048-token sequences
+
+
+def bench_stack(device, steps, warmup, rank=0, world=1, group=None, barrier=None, layers=48):
+    """the Qwen3-30B-A3B-shaped 48-layer stack (random-init
+    MXFP4 weights for every linear).  Prefill of 8 x 2048 tokens (eager, CUDA
+    events) and decode steps of one token per sequence at batch 1..256 over a
+    2048-token KV cache (one CUDA graph per step, replayed); tokens/s of the
+    whole job, max over ranks.  On several GPUs: dense linears column-sharded,
+    experts expert-parallel, attention sharded by sequence."""
+    dsm = _load("mxfp4_decoder_stack", PKG / "decoder_stack.py")
+    cfg = dsm.StackConfig(layers=layers)
+    full = [dsm.random_layer(cfg, device, seed=1000 + i) for i in range(cfg.layers)]
+    stack = dsm.DecoderStack(cfg, full, rank=rank, world=world, group=group,
+                             max_ctx=max(STACK_PREFILL[1], STACK_DECODE_CTX) + 8,
+                             max_tokens=STACK_PREFILL[0] * STACK_PREFILL[1])
+    del full
+    torch.cuda.empty_cache()
+    sync = barrier if barrier is not None else (lambda: None)
+    out = {}
+    seqs, seq_len = STACK_PREFILL
+    g = torch.Generator(device=device).manual_seed(77)
+    h = torch.randn(seqs * seq_len, cfg.hidden, generator=g, device=device).to(torch.bfloat16)
+    stack.allocate_cache(seqs, seq_len)
+    for _ in range(warmup):
+        stack.prefill(h, seqs)
+    torch.cuda.synchronize()
+    sync()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(steps):
+        stack.prefill(h, seqs)
+    en.record()
+    en.synchronize()
+    ms = st.elapsed_time(en) / steps
+    if world > 1:
+        ms = _max_over_ranks(ms, device)
+    tokens = seqs * seq_len
+    fl = cfg.layers * cfg.layer_flops(tokens, dsm.attention_ctx_per_token(seq_len, 0))
+    out["prefill"] = {"tokens": tokens, "ms": ms, "tokens_per_s": tokens / (ms * 1e-3),
+                      "tflops": fl / (ms * 1e-3) / 1e12, "what": f"{seqs} x {seq_len} tokens, {cfg.layers} layers"}
+    del h
+    for b in STACK_DECODE_BATCHES:
+        stack.allocate_cache(b, STACK_DECODE_CTX + 1)
+        hb = torch.randn(b, cfg.hidden, generator=g, device=device).to(torch.bfloat16)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                stack.decode(hb, STACK_DECODE_CTX)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            stack.decode(hb, STACK_DECODE_CTX)
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        sync()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(steps):
+            graph.replay()
+        en.record()
+        en.synchronize()
+        ms = st.elapsed_time(en) / steps
+        if world > 1:
+            ms = _max_over_ranks(ms, device)
+        out[f"decode_b{b}"] = {"ms": ms, "tokens_per_s": b / (ms * 1e-3), "context": STACK_DECODE_CTX}
+        del graph, hb
+        torch.cuda.synchronize()
+        sync()
+    stack.cache = None
+    del stack
+    torch.cuda.empty_cache()
+    out["config"] = {"layers": cfg.layers, "hidden": cfg.hidden, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
+                     "head_dim": cfg.head_dim, "experts": cfg.experts, "top_k": cfg.top_k, "inter": cfg.inter,
+                     "attention": "torch SDPA", "parallelism": "single GPU" if world == 1 else
+                     f"tp{world} dense (fused all-gather) + ep{world} experts + sequence-sharded attention"}
+    return out
+
+
 def moe_flops(cfg=MOE):
     return 2.0 * cfg["t"] * cfg["k"] * (cfg["h"] * 2 * cfg["inter"] + cfg["inter"] * cfg["h"])
 
@@ -670,6 +754,7 @@ def main():
         rbytes = MOE["t"] * MOE["e"] * 4 + MOE["t"] * MOE["k"] * 8
         extra["config2_router"] = {"ms": ms_r, "us": ms_r * 1e3, "gbs": rbytes / ms_r / 1e6,
                                    "what": "softmax + top-8 + renormalise over 128 expert logits, 4096 tokens"}
+        extra["config4_stack"] = bench_stack(device, 3, 1)
         ms_w = bench_w4a4(soft, 50, 5, device)
         fw = 2.0 * W4A4[0] * W4A4[1] * W4A4[2]
         extra["config3_w4a4"] = {"ms": ms_w, "tflops": fw / ms_w / 1e9,
@@ -910,6 +995,7 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
     parity = {"tp": bool(flags[0]), "tp_nccl": bool(flags[1]), "ep": bool(flags[2]), "ep_nccl": bool(flags[3]),
               "what": "each rank's output vs the single-GPU call on the same inputs, bit for bit, min over ranks"}
     t_ep_roof = max(fm / world / (pk["bf16_tflops"] * 1e12), ep_nv_bytes / (NVLINK_GBS * 1e9))
+    stack = bench_stack(device, 3, 1, rank=rank, world=world, barrier=barrier)
     status = soft.device_status()
     status = int(_max_over_ranks(float(status), device))
 
@@ -947,7 +1033,8 @@ def run_sharded(args, soft, world, rank, device, pk, pk_kind):
                 "timing": ("CUDA graph of rotating input sets (expert weights > L2) replayed, CUDA events, "
                            "max over ranks") if ep_timing == "graph" else "CUDA events around eager calls, max over ranks"},
                 "config2_moe_layer_ep_nccl": {"ms": ms_ep_nccl, "tokens_per_s": MOE["t"] / (ms_ep_nccl * 1e-3),
-                                              "what": "NCCL all-to-all dispatch/combine (host syncs on counts)"}},
+                                              "what": "NCCL all-to-all dispatch/combine (host syncs on counts)"},
+                "config4_stack": stack},
         }
         if status:
             line["device_status"] = status

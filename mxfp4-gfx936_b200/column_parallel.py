@@ -113,9 +113,23 @@ class _SymmBuffer:
         self.local = None
 
 
+class _OutputState:
+    """The two alternating output buffers of fused column-parallel calls, the
+    device barrier that ends each call, and the call count that alternates
+    them.  Layers that run one after another in stream order on every rank
+    (the linears of a decoder stack) can share one state: a call's result
+    stays valid until the second call after it through the same state."""
+
+    def __init__(self):
+        self.bufs = None
+        self.barrier = None
+        self.step = 0
+
+
 class ColumnParallelLinear:
     def __init__(self, w_shard: torch.Tensor, s_shard: torch.Tensor, n_full: int, rank: int, world: int,
-                 group=None, linear_fn=None, fused: bool = False, multicast: bool | None = None):
+                 group=None, linear_fn=None, fused: bool = False, multicast: bool | None = None,
+                 buffer_pool: dict | None = None):
         self.w, self.s = w_shard.contiguous(), s_shard.contiguous()
         self.n_full, self.rank, self.world, self.group = n_full, rank, world, group
         self.linear_fn = linear_fn if linear_fn is not None else _soft().linear_mxfp4_soft
@@ -125,15 +139,16 @@ class ColumnParallelLinear:
             raise ValueError("the fused all-gather runs the native kernel; linear_fn cannot be injected")
         self.fused = fused and world > 1
         self.multicast = multicast  # None: NVSwitch multicast for groups of >= MULTICAST_MIN_WORLD GPUs
-        self._bufs = None      # two output buffers [rows, n_full]: _SymmBuffer or PeerBuffers
-        self._barrier = None
-        self._step = 0
+        # output buffers per (output width, dtype): this layer's own, or shared
+        # with the other layers given the same pool (same group, same stream order)
+        self._pool = buffer_pool if buffer_pool is not None else {}
+        self._bufs = None      # the last call's two output buffers [rows, n_full]: _SymmBuffer or PeerBuffers
 
     @classmethod
     def from_full(cls, w: torch.Tensor, s: torch.Tensor, rank: int, world: int, group=None, linear_fn=None,
-                  fused: bool = False, multicast: bool | None = None):
+                  fused: bool = False, multicast: bool | None = None, buffer_pool: dict | None = None):
         lo, hi = shard_rows(w.shape[0], rank, world)
-        return cls(w[lo:hi], s[lo:hi], w.shape[0], rank, world, group, linear_fn, fused, multicast)
+        return cls(w[lo:hi], s[lo:hi], w.shape[0], rank, world, group, linear_fn, fused, multicast, buffer_pool)
 
     def _alloc(self, m: int, dtype: torch.dtype, device: torch.device):
         """Two output buffers [m, n_full]; collective over the group."""
@@ -156,16 +171,18 @@ class ColumnParallelLinear:
         n_local = self.w.shape[0]
         if x2.dtype not in (torch.bfloat16, torch.float16):
             raise TypeError("x must be BF16 or FP16")
-        if self._bufs is None or self._bufs[0].local.shape[0] < m or self._bufs[0].local.dtype != x2.dtype:
+        st = self._pool.setdefault((self.n_full, x2.dtype), _OutputState())
+        if st.bufs is None or st.bufs[0].local.shape[0] < m:
             # collective: every rank of a TP group sees the same M
-            if self._bufs is not None:
-                for b in self._bufs:
+            if st.bufs is not None:
+                for b in st.bufs:
                     b.close(self.group)  # collective: every rank reallocates at the same call
-            self._bufs = self._alloc(m, x2.dtype, x2.device)
-            if self._barrier is None:
-                self._barrier = pm.PeerBarrier(self.group)
-        buf = self._bufs[self._step % 2]
-        self._step += 1
+            st.bufs = self._alloc(m, x2.dtype, x2.device)
+            if st.barrier is None:
+                st.barrier = pm.PeerBarrier(self.group)
+        self._bufs = st.bufs
+        buf = st.bufs[st.step % 2]
+        st.step += 1
         esz = x2.element_size()
         col = self.rank * n_local * esz
         peers = [buf.ptrs[j] + col for j in range(self.world) if j != self.rank]
@@ -189,7 +206,7 @@ class ColumnParallelLinear:
                     soft._check(lib.mxfp4_linear_w4a16_allgather_mc(*common, ctypes.c_void_p(mc + col), *tail))
                 else:
                     soft._check(lib.mxfp4_linear_w4a16_allgather(*common, *tail))
-        self._barrier()
+        st.barrier()
         return buf.local[:m]
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:

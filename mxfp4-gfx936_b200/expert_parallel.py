@@ -91,7 +91,8 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, w13_local, s13_local, w2_local, s2_local, num_experts: int, rank: int, world: int,
-                 group=None, layer_fn=None, route_fn=None, fused: bool | None = None, max_tokens: int | None = None):
+                 group=None, layer_fn=None, route_fn=None, fused: bool | None = None, max_tokens: int | None = None,
+                 buffer_pool: dict | None = None):
         self.w13, self.s13, self.w2, self.s2 = w13_local, s13_local, w2_local, s2_local
         self.num_experts, self.rank, self.world, self.group = num_experts, rank, world, group
         self.lo, self.hi = expert_range(num_experts, rank, world)
@@ -107,14 +108,20 @@ class ExpertParallelMoE:
         self.max_tokens = max_tokens
         self.layer_fn = layer_fn if layer_fn is not None else _soft().moe_layer_mxfp4
         self.route_fn = route_fn if route_fn is not None else self._device_route
-        self._peer = None  # (top_k, capacity, counts, xr, wr, yr, barrier) once allocated
+        self._peer = None  # (top_k, capacity, counts, xr, wr, yr, barrier, tables, max_tokens) once allocated
+        # peer buffers keyed by (top_k, hidden): this layer's own, or shared with
+        # the other layers given the same pool.  Layers that run one after another
+        # in stream order on every rank can share them: each call's three device
+        # barriers order its buffer uses against the previous call's.
+        self._pool = buffer_pool if buffer_pool is not None else {}
 
     @classmethod
     def from_full(cls, w13, s13, w2, s2, rank: int, world: int, group=None, layer_fn=None, route_fn=None,
-                  fused: bool | None = None, max_tokens: int | None = None):
+                  fused: bool | None = None, max_tokens: int | None = None, buffer_pool: dict | None = None):
         lo, hi = expert_range(w13.shape[0], rank, world)
         return cls(w13[lo:hi].contiguous(), s13[lo:hi].contiguous(), w2[lo:hi].contiguous(),
-                   s2[lo:hi].contiguous(), w13.shape[0], rank, world, group, layer_fn, route_fn, fused, max_tokens)
+                   s2[lo:hi].contiguous(), w13.shape[0], rank, world, group, layer_fn, route_fn, fused, max_tokens,
+                   buffer_pool)
 
     # ------------------------------------------------------------------ fused (native) path
     def _peer_buffers(self, t: int, top_k: int, hidden: int):
@@ -125,6 +132,11 @@ class ExpertParallelMoE:
             if self._peer[0] != top_k:
                 raise ValueError("top_k changed between calls of a fused expert-parallel layer")
             return self._peer
+        shared = self._pool.get((top_k, hidden))
+        if shared is not None:
+            self._peer = shared
+            self.max_tokens = shared[8]
+            return shared
         pm = _peer_memory()
         if self.max_tokens is None:
             n = torch.tensor([t], dtype=torch.int64, device=self.w13.device)
@@ -138,7 +150,8 @@ class ExpertParallelMoE:
         yr = pm.PeerBuffers((cap, hidden), torch.bfloat16, self.group)
         barrier = pm.PeerBarrier(self.group)
         tables = [pm.pointer_array(b.ptrs) for b in (counts, xr, wr, yr)]
-        self._peer = (top_k, cap, counts, xr, wr, yr, barrier, tables)
+        self._peer = (top_k, cap, counts, xr, wr, yr, barrier, tables, self.max_tokens)
+        self._pool[(top_k, hidden)] = self._peer
         return self._peer
 
     def _fused_call(self, x, topk_weights, topk_ids):
@@ -150,7 +163,7 @@ class ExpertParallelMoE:
             raise TypeError(f"x must be bf16, got {x.dtype}")
         if topk_ids.shape != topk_weights.shape or topk_ids.shape[0] != t:
             raise ValueError("top-k ids and weights must have matching (M, top_k) shapes")
-        top_k_, cap, counts, xr, wr, yr, barrier, tables = self._peer_buffers(t, top_k, hidden)
+        top_k_, cap, counts, xr, wr, yr, barrier, tables, _ = self._peer_buffers(t, top_k, hidden)
         if t > self.max_tokens:
             raise ValueError(f"{t} tokens exceed the {self.max_tokens} this expert-parallel layer was sized for")
         inter = self.w13.shape[1] // 2
