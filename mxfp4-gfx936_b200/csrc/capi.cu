@@ -10,6 +10,7 @@
 #include "ep.cuh"
 #include "gemm.cuh"
 #include "gemm2.cuh"
+#include "gemm_routed.cuh"
 #include "gemm_small.cuh"
 #include "gemm_w4a4.cuh"
 
@@ -206,6 +207,32 @@ int launch_small(const CUtensorMap& tx, const CUtensorMap& tw, const SmallParams
   return MXFP4_OK;
 }
 
+// Fused few-token linear with the decoded weights in tensor memory (the same
+// K split, MMA order and reduction as launch_small's kernel).
+template <bool FP16>
+int launch_small_tmem(const CUtensorMap& tx, const CUtensorMap& tw, const SmallParams& p, cudaStream_t stream) {
+  auto kern = mxfp4_linear_small_tmem_kernel<FP16>;
+  const int data = kTmXSlots * p.mp * 128 + kTmPSlots * kTmPGroupBytes;
+  const int part = kSmRows * p.mp * 4;
+  const int bars = (2 * kTmPSlots + 2 * kTmXSlots + 2 * kTmASlots + 2) * 8;
+  const int smem = ((data > part ? data : part) + 15) / 16 * 16 + bars + 64 + 1024;
+  MX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.ks, (p.N + kSmRows - 1) / kSmRows, 1);
+  cfg.blockDim = dim3(256 + 32 * kTmDecodeWarps, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MX_CUDA(cudaLaunchKernelEx(&cfg, kern, tx, tw, p));
+  return MXFP4_OK;
+}
+
 template <int BMODE, bool FP16>
 int launch_gemv(const GemvParams& g, int sms, cudaStream_t stream) {
   const int mr = g.M <= 1 ? 1 : 2;
@@ -266,7 +293,8 @@ int64_t route_capacity(int64_t num_routes, int num_experts, int block_m) {
 
 int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_experts,
               int expert_offset, int block_m, int32_t* sorted_ids, int32_t* block_expert,
-              int32_t* post, int64_t capacity, uint8_t* ws, cudaStream_t stream) {
+              int32_t* post, int64_t capacity, uint8_t* ws, cudaStream_t stream,
+              int4* rt_chunks = nullptr, int32_t* rt_num_chunks = nullptr) {
   RouteWs r = carve_route_ws(ws, num_routes, num_experts);
   const int64_t chunks = std::max<int64_t>((num_routes + kRouteThreads - 1) / kRouteThreads, 1);
   const size_t smem = sizeof(int32_t) * kRouteWarps * num_experts;
@@ -285,7 +313,7 @@ int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_expert
   MX_CUDA(cudaGetLastError());
   route_offsets_kernel<<<1, 1024, 0, stream>>>(r.hist, static_cast<int>(chunks), num_experts, block_m,
                                                num_routes, r.blk_off, sorted_ids, block_expert, post,
-                                               capacity / block_m);
+                                               capacity / block_m, rt_chunks, rt_num_chunks, kRtChunkBlocks);
   MX_CUDA(cudaGetLastError());
   if (num_routes > 0)
     route_scatter_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, 0, stream>>>(
@@ -293,6 +321,90 @@ int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_expert
         sorted_ids);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
+}
+
+// --- routing of the routed GEMMs (32-route blocks, chunks of <= 256 routes) ---
+int64_t rt_max_chunks(int64_t routes, int num_experts) {
+  const int64_t cap = route_capacity(routes, num_experts, kRtBlock);
+  return cap / (kRtBlock * kRtChunkBlocks) + std::min<int64_t>(num_experts, routes) + 1;
+}
+
+struct RtRouting {
+  int64_t cap;         // padded routed rows
+  int64_t max_chunks;
+  int32_t* sorted;     // [cap]
+  int32_t* block_expert;
+  int32_t* post;
+  int4* chunks;        // [max_chunks]
+  int32_t* num_chunks;
+  uint8_t* route_ws;
+};
+
+size_t rt_routing_bytes(int64_t routes, int num_experts) {
+  const int64_t cap = route_capacity(routes, num_experts, kRtBlock);
+  return align_up(sizeof(int32_t) * std::max<int64_t>(cap, 1), 256) + align_up(sizeof(int32_t) * (cap / kRtBlock + 1), 256) +
+         256 + align_up(sizeof(int4) * rt_max_chunks(routes, num_experts), 256) + 256 + route_ws_bytes(routes, num_experts);
+}
+
+RtRouting carve_rt_routing(uint8_t*& ws, int64_t routes, int num_experts) {
+  RtRouting r;
+  r.cap = route_capacity(routes, num_experts, kRtBlock);
+  r.max_chunks = rt_max_chunks(routes, num_experts);
+  r.sorted = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * std::max<int64_t>(r.cap, 1), 256);
+  r.block_expert = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * (r.cap / kRtBlock + 1), 256);
+  r.post = reinterpret_cast<int32_t*>(ws);
+  ws += 256;
+  r.chunks = reinterpret_cast<int4*>(ws);
+  ws += align_up(sizeof(int4) * r.max_chunks, 256);
+  r.num_chunks = reinterpret_cast<int32_t*>(ws);
+  ws += 256;
+  r.route_ws = ws;
+  ws += route_ws_bytes(routes, num_experts);
+  return r;
+}
+
+int run_rt_routing(const void* ids, int ids_dtype, int64_t routes, int num_experts, const RtRouting& r,
+                   cudaStream_t s) {
+  return run_route(ids, ids_dtype, routes, num_experts, 0, kRtBlock, r.sorted, r.block_expert, r.post, r.cap,
+                   r.route_ws, s, r.chunks, r.num_chunks);
+}
+
+template <int EPI, bool FP16>
+int launch_routed(const CUtensorMap& tw, const CUtensorMap& tx16, const CUtensorMap& tx128, const RoutedParams& p,
+                  int sms, cudaStream_t stream) {
+  auto kern = mxfp4_routed_tmem_kernel<EPI, FP16>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmemBytes);
+  });
+  MX_CUDA(attr_err);
+  const int64_t tiles = static_cast<int64_t>(p.max_chunks) * p.num_wblocks;
+  const int clusters = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms / 2)));
+  kern<<<2 * clusters, kRtThreads, kRtSmemBytes, stream>>>(tw, tx16, tx128, p);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+// Stages per packed-weight TMA load of a routed GEMM: 4 when they divide the
+// weights' 64-K stage count, else 2 (K is a multiple of 128).
+int routed_pgroup(int64_t kw) { return (kw / kP2BK) % 4 == 0 ? 4 : 2; }
+
+// The three tensor maps of a routed GEMM: packed weights [rows_total, kw/2]
+// (boxes of pgroup stages x 128 rows, GLU: x 64 rows) and the routed
+// activations [cap, ka] in 16-row and 128-row boxes.
+int routed_maps(CUtensorMap* tw, CUtensorMap* tx16, CUtensorMap* tx128, const void* w, int64_t rows_total, int64_t kw,
+                const void* xr, int64_t cap, int64_t ka, bool fp16, bool glu) {
+  const CUtensorMapDataType xt = fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint32_t box_bytes = static_cast<uint32_t>(routed_pgroup(kw) * (kP2BK / 2));
+  if (int rc = make_map_2d(tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, kw / 2, rows_total, kw / 2, box_bytes,
+                           glu ? 64 : 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  const uint64_t rows = static_cast<uint64_t>(std::max<int64_t>(cap, 1));
+  if (int rc = make_map_2d(tx16, xr, xt, 2, ka, rows, ka * 2, kP2BK, 16, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
+  return make_map_2d(tx128, xr, xt, 2, ka, rows, ka * 2, kP2BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace
@@ -545,11 +657,11 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
     q.bias = bias;
     if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kSmBK, q.mp, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
     if (mode == MXFP4_LINEAR_FUSED && wd == nullptr) {
-      if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw, kSmBK / 2, kSmRows,
-                               CU_TENSOR_MAP_SWIZZLE_NONE))
+      if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw,
+                               kTmPGroup * (kSmBK / 2), kSmRows, CU_TENSOR_MAP_SWIZZLE_NONE))
         return rc;
-      if (fp16) return push(launch_small<B_DECODE, true>(ta, tb, q, s));
-      return push(launch_small<B_DECODE, false>(ta, tb, q, s));
+      if (fp16) return push(launch_small_tmem<true>(ta, tb, q, s));
+      return push(launch_small_tmem<false>(ta, tb, q, s));
     }
     if (wd == nullptr)
       if (int rc = dequant_into_workspace()) return rc;
@@ -877,22 +989,18 @@ MoeCompute moe_compute(int a_dtype, int c_dtype) {
 
 extern "C" {
 
-// Workspace of the routed op: routing arrays, routing scratch, converted A,
-// activations in routed order.
+// Workspace of the routed op: routing arrays and chunk table, routing
+// scratch, converted A, activations in routed order.
 size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t n,
                                       int64_t k, int a_dtype, int c_dtype) {
   (void)n;
   const int64_t routes = num_tokens * top_k;
-  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
+  const int64_t cap = route_capacity(routes, num_experts, kRtBlock);
   const MoeCompute mc = moe_compute(a_dtype, c_dtype);
   const int64_t ka = k * mc.parts;  // columns of the converted activations
-  size_t b = 0;
-  b += align_up(sizeof(int32_t) * cap, 256);
-  b += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
-  b += 256;  // num_post_padded
-  b += route_ws_bytes(routes, num_experts);
+  size_t b = rt_routing_bytes(routes, num_experts);
   if (a_dtype != mc.dtype || mc.parts > 1) b += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
-  b += align_up(static_cast<size_t>(cap) * ka * 2, 256);  // activations in routed order
+  b += align_up(static_cast<size_t>(std::max<int64_t>(cap, 1)) * ka * 2, 256);  // activations in routed order
   return b;
 }
 
@@ -933,15 +1041,7 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   MX_CUDA(cudaMemsetAsync(C, 0, static_cast<size_t>(routes) * n * esz, s));
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
-  int32_t* sorted_ids = reinterpret_cast<int32_t*>(ws);
-  ws += align_up(sizeof(int32_t) * cap, 256);
-  int32_t* block_expert = reinterpret_cast<int32_t*>(ws);
-  ws += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
-  int32_t* post = reinterpret_cast<int32_t*>(ws);
-  ws += 256;
-  uint8_t* route_ws = ws;
-  ws += route_ws_bytes(routes, num_experts);
+  const RtRouting rt = carve_rt_routing(ws, routes, num_experts);
   const void* a_eff = A;
   if (a_dtype == MXFP4_DTYPE_U8) {
     if (int rc = mxfp4_dequant(A, a_mx_scale, ws, cdt, num_tokens, k, stream)) return rc;
@@ -959,36 +1059,29 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
     MX_CUDA(cudaGetLastError());
     a_eff = ws;
   }
-  if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kP2BM, sorted_ids, block_expert, post, cap,
-                         route_ws, s))
-    return rc;
+  if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
   MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
   if (a_eff != A) ws += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
   void* a_routed = ws;
-  if (int rc = run_gather(a_eff, ka, sorted_ids, post, routes, top_k, a_routed, cap, info.sms, s)) return rc;
+  if (int rc = run_gather(a_eff, ka, rt.sorted, rt.post, routes, top_k, a_routed, rt.cap, info.sms, s)) return rc;
 
-  CUtensorMap ta, tb;
-  const CUtensorMapDataType at = cdt == MXFP4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  if (int rc = make_map_2d(&ta, a_routed, at, 2, ka, cap, ka * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+  CUtensorMap tw, tx16, tx128;
+  if (int rc = routed_maps(&tw, &tx16, &tx128, B, static_cast<int64_t>(num_experts) * n, k, a_routed, rt.cap, ka,
+                           cdt == MXFP4_DTYPE_F16, false))
     return rc;
-  if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, static_cast<uint64_t>(num_experts) * n,
-                           k / 2, kP2BK / 2, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_NONE))
-    return rc;
-  PairParams p{};
+  RoutedParams p{};
+  p.pgroup = routed_pgroup(k);
   p.N = static_cast<int>(n);
   p.K = static_cast<int>(ka);
   p.k_rep = mc.parts;
-  p.bn = 256;
-  p.num_m_blocks = static_cast<int>(cap / kP2BM);
-  p.num_n_blocks = static_cast<int>((n + p.bn - 1) / p.bn);
-  p.a_ptr = static_cast<const uint8_t*>(a_eff);
-  p.lda = ka;
+  p.num_wblocks = static_cast<int>((n + 255) / 256);
   p.w_scales = static_cast<const uint8_t*>(B_mx_scale);
   p.lds = k / 32;
   p.w_rows_per_expert = n;
-  p.sorted_ids = sorted_ids;
-  p.block_expert = block_expert;
-  p.num_post_padded = post;
+  p.chunks = rt.chunks;
+  p.num_chunks = rt.num_chunks;
+  p.max_chunks = static_cast<int>(rt.max_chunks);
+  p.sorted_ids = rt.sorted;
   p.num_routes = static_cast<int>(routes);
   p.top_k = top_k;
   p.out = C;
@@ -1000,8 +1093,8 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   p.mul_w = mul_routed_weight ? 1 : 0;
   p.c_stride_t = static_cast<int64_t>(top_k) * n;
   p.c_stride_j = n;
-  p.vec_ok = aligned(C, 16) && (n * esz) % 16 == 0;
-  return routed_pair_gemm<A_TMA, EPI_MOE>(cdt == MXFP4_DTYPE_F16, ta, tb, p, info.sms, s);
+  if (cdt == MXFP4_DTYPE_F16) return launch_routed<EPI_MOE, true>(tw, tx16, tx128, p, info.sms, s);
+  return launch_routed<EPI_MOE, false>(tw, tx16, tx128, p, info.sms, s);
 }
 
 // Same operation as mxfp4_fused_moe, with its scratch taken from the static
@@ -1136,15 +1229,11 @@ int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const vo
 size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t hidden,
                                       int64_t inter) {
   const int64_t routes = num_tokens * top_k;
-  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
-  size_t b = 0;
-  b += align_up(sizeof(int32_t) * cap, 256);
-  b += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
-  b += 256;
-  b += route_ws_bytes(routes, num_experts);
-  b += align_up(static_cast<size_t>(cap) * inter * 2, 256);     // h in routed order
-  b += align_up(static_cast<size_t>(routes) * hidden * 2, 256); // weighted down rows
-  b += align_up(static_cast<size_t>(cap) * hidden * 2, 256);    // x in routed order
+  const int64_t cap = std::max<int64_t>(route_capacity(routes, num_experts, kRtBlock), 1);
+  size_t b = rt_routing_bytes(routes, num_experts);
+  b += align_up(static_cast<size_t>(cap) * inter * 2, 256);                           // h in routed order
+  b += align_up(static_cast<size_t>(std::max<int64_t>(routes, 1)) * hidden * 2, 256);  // weighted down rows
+  b += align_up(static_cast<size_t>(cap) * hidden * 2, 256);                          // x in routed order
   return b;
 }
 
@@ -1169,95 +1258,72 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   cudaStream_t s = as_stream(stream);
   const int64_t routes = num_tokens * top_k;
   if (num_tokens == 0) return MXFP4_OK;
-  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  int32_t* sorted_ids = reinterpret_cast<int32_t*>(ws);
-  ws += align_up(sizeof(int32_t) * cap, 256);
-  int32_t* block_expert = reinterpret_cast<int32_t*>(ws);
-  ws += align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256);
-  int32_t* post = reinterpret_cast<int32_t*>(ws);
-  ws += 256;
-  uint8_t* route_ws = ws;
-  ws += route_ws_bytes(routes, num_experts);
+  const RtRouting rt = carve_rt_routing(ws, routes, num_experts);
+  const int64_t cap = std::max<int64_t>(rt.cap, 1);
   void* hbuf = ws;
   ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
   void* ybuf = ws;
   ws += align_up(static_cast<size_t>(routes) * hidden * 2, 256);
   void* xbuf = ws;
 
-  if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kP2BM, sorted_ids, block_expert, post, cap,
-                         route_ws, s))
-    return rc;
-  if (int rc = run_gather(x, hidden, sorted_ids, post, routes, top_k, xbuf, cap, info.sms, s)) return rc;
+  if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
+  if (int rc = run_gather(x, hidden, rt.sorted, rt.post, routes, top_k, xbuf, rt.cap, info.sms, s)) return rc;
 
   // gate_up with fused SiLU(gate) * up -> h [cap, inter] in routed order
   {
-    CUtensorMap ta, tb;
-    if (int rc = make_map_2d(&ta, xbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hidden, cap, hidden * 2, kP2BK,
-                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    CUtensorMap tw, tx16, tx128;
+    if (int rc = routed_maps(&tw, &tx16, &tx128, w13, static_cast<int64_t>(num_experts) * 2 * inter, hidden, xbuf,
+                             cap, hidden, false, true))
       return rc;
-    if (int rc = make_map_2d(&tb, w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hidden / 2,
-                             static_cast<uint64_t>(num_experts) * 2 * inter, hidden / 2, kP2BK / 2, kP2HalfRows,
-                             CU_TENSOR_MAP_SWIZZLE_NONE))
-      return rc;
-    PairParams p{};
+    RoutedParams p{};
+    p.pgroup = routed_pgroup(hidden);
     p.N = static_cast<int>(2 * inter);
+    p.glu_inter = static_cast<int>(inter);
     p.K = static_cast<int>(hidden);
-    p.bn = 256;
-    p.num_m_blocks = static_cast<int>(cap / kP2BM);
-    p.num_n_blocks = static_cast<int>((inter + p.bn / 2 - 1) / (p.bn / 2));
-    p.a_ptr = static_cast<const uint8_t*>(x);
-    p.lda = hidden;
+    p.num_wblocks = static_cast<int>((inter + 127) / 128);
     p.w_scales = static_cast<const uint8_t*>(w13_scale);
     p.lds = hidden / 32;
     p.w_rows_per_expert = 2 * inter;
-    p.glu_inter = static_cast<int>(inter);
-    p.sorted_ids = sorted_ids;
-    p.block_expert = block_expert;
-    p.num_post_padded = post;
+    p.chunks = rt.chunks;
+    p.num_chunks = rt.num_chunks;
+    p.max_chunks = static_cast<int>(rt.max_chunks);
+    p.sorted_ids = rt.sorted;
     p.num_routes = static_cast<int>(routes);
     p.top_k = top_k;
     p.out = hbuf;
     p.ldo = inter;
     p.out_dtype = MXFP4_DTYPE_BF16;
-    p.vec_ok = 1;
-    if (int rc = routed_pair_gemm<A_TMA, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
+    if (int rc = launch_routed<EPI_GLU, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
   }
   // down with route weights, scattered to y[route] = [routes, hidden]
   {
-    CUtensorMap ta, tb;
-    if (int rc = make_map_2d(&ta, hbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inter, cap, inter * 2, kP2BK,
-                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    CUtensorMap tw, tx16, tx128;
+    if (int rc = routed_maps(&tw, &tx16, &tx128, w2, static_cast<int64_t>(num_experts) * hidden, inter, hbuf, cap,
+                             inter, false, false))
       return rc;
-    if (int rc = make_map_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inter / 2,
-                             static_cast<uint64_t>(num_experts) * hidden, inter / 2, kP2BK / 2, kP2HalfRows,
-                             CU_TENSOR_MAP_SWIZZLE_NONE))
-      return rc;
-    PairParams p{};
+    RoutedParams p{};
+    p.pgroup = routed_pgroup(inter);
     p.N = static_cast<int>(hidden);
     p.K = static_cast<int>(inter);
-    p.bn = 256;
-    p.num_m_blocks = static_cast<int>(cap / kP2BM);
-    p.num_n_blocks = static_cast<int>((hidden + p.bn - 1) / p.bn);
+    p.num_wblocks = static_cast<int>((hidden + 255) / 256);
     p.w_scales = static_cast<const uint8_t*>(w2_scale);
     p.lds = inter / 32;
     p.w_rows_per_expert = hidden;
-    p.sorted_ids = sorted_ids;
-    p.block_expert = block_expert;
-    p.num_post_padded = post;
+    p.chunks = rt.chunks;
+    p.num_chunks = rt.num_chunks;
+    p.max_chunks = static_cast<int>(rt.max_chunks);
+    p.sorted_ids = rt.sorted;
     p.num_routes = static_cast<int>(routes);
     p.top_k = 1;
     p.out = ybuf;
     p.out_dtype = MXFP4_DTYPE_BF16;
-    p.a_scale = nullptr;
-    p.b_scale = nullptr;
     p.topk_w = topk_weights;
     p.w_dtype = w_dtype;
     p.mul_w = 1;
     p.c_stride_t = hidden;
     p.c_stride_j = 0;
-    p.vec_ok = 1;
-    if (int rc = routed_pair_gemm<A_TMA, EPI_MOE>(false, ta, tb, p, info.sms, s)) return rc;
+    if (int rc = launch_routed<EPI_MOE, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
   }
   const int64_t vecs = num_tokens * (hidden / 8);
   const int grid = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, int64_t(info.sms) * 8));
@@ -1272,6 +1338,17 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
 // ---------------------------------------------------------------------------
 // Expert-parallel MoE layer (csrc/ep.cuh).
 // ---------------------------------------------------------------------------
+}  // extern "C"
+
+namespace {
+// Route chunks of an owner's received rows (all E experts bound the local ones).
+int64_t ep_max_chunks(int64_t recv_capacity, int num_experts) {
+  return recv_capacity / (kEpBlock * kEpChunkBlocks) + num_experts + 1;
+}
+}  // namespace
+
+extern "C" {
+
 int64_t mxfp4_ep_moe_recv_capacity(int64_t max_tokens_per_rank, int top_k, int num_experts, int world) {
   if (max_tokens_per_rank < 0 || top_k <= 0 || num_experts <= 0 || world <= 0 || num_experts % world) return 0;
   const int64_t el = num_experts / world;
@@ -1286,6 +1363,8 @@ size_t mxfp4_ep_moe_workspace_size(int64_t num_tokens, int top_k, int num_expert
   b += align_up(sizeof(int32_t) * num_experts, 256) * 2;                  // send_base, lstart
   b += align_up(sizeof(int32_t) * (recv_capacity / kEpBlock + 1), 256);   // owner block experts
   b += 256;                                                               // owner used rows
+  b += align_up(sizeof(int4) * ep_max_chunks(recv_capacity, num_experts), 256);  // owner route chunks
+  b += 256;                                                               // number of chunks
   b += align_up(sizeof(int32_t) * std::max<int64_t>(recv_capacity, 1), 256);  // owner row ids
   b += align_up(sizeof(int32_t) * std::max<int64_t>(routes, 1), 256) * 3; // sorted, expert per position, dst
   b += 256;                                                               // valid routes
@@ -1314,7 +1393,7 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
   MX_CHECK(ids_dtype == MXFP4_DTYPE_I32 || ids_dtype == MXFP4_DTYPE_I64, "topk_ids must be I32 or I64");
   MX_CHECK(aligned(x, 16) && aligned(out, 16), "x and out must be 16-byte aligned");
   MX_CHECK(recv_capacity > 0 && recv_capacity % kEpBlock == 0 && recv_capacity < (int64_t(1) << 24),
-           "recv_capacity must be a positive multiple of 256 below 2^24");
+           "recv_capacity must be a positive multiple of 32 below 2^24");
   const int64_t routes = num_tokens * top_k;
   MX_CHECK(static_cast<int64_t>(world) * routes + (num_experts / world) * (kEpBlock - 1) <= recv_capacity ||
                routes == 0,
@@ -1347,6 +1426,9 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
   int32_t* lstart = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * num_experts));
   int32_t* block_expert = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (cap_blocks + 1)));
   int32_t* post = reinterpret_cast<int32_t*>(take(256));
+  const int64_t max_chunks = ep_max_chunks(cap, num_experts);
+  int4* chunks = reinterpret_cast<int4*>(take(sizeof(int4) * max_chunks));
+  int32_t* nchunks = reinterpret_cast<int32_t*>(take(256));
   int32_t* rid = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * cap));
   int32_t* sorted = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(routes, 1)));
   int32_t* bexp = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(routes, 1)));
@@ -1362,7 +1444,7 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
   MX_CUDA(cudaGetLastError());
   // 2. plan + stable local order; dispatch rows into the owners' xr; barrier
   ep_plan_kernel<<<1, 1024, 0, s>>>(static_cast<const int32_t*>(counts[rank]), num_experts, world, rank, send_base,
-                                    lstart, block_expert, post, rid, static_cast<int>(cap), cap_blocks);
+                                    lstart, block_expert, post, rid, static_cast<int>(cap), cap_blocks, chunks, nchunks);
   MX_CUDA(cudaGetLastError());
   if (routes > 0) {
     if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, 1, sorted, bexp, nvalid, routes, route_ws, s))
@@ -1377,56 +1459,47 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
   MX_CUDA(cudaGetLastError());
   // 3. owner: gate_up (fused SiLU * up) and down (route weight) over the received rows
   {
-    CUtensorMap ta, tb;
-    if (int rc = make_map_2d(&ta, xr[rank], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hidden, cap, hidden * 2, kP2BK,
-                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    CUtensorMap tw, tx16, tx128;
+    if (int rc = routed_maps(&tw, &tx16, &tx128, w13, static_cast<int64_t>(el) * 2 * inter, hidden, xr[rank], cap,
+                             hidden, false, true))
       return rc;
-    if (int rc = make_map_2d(&tb, w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hidden / 2,
-                             static_cast<uint64_t>(el) * 2 * inter, hidden / 2, kP2BK / 2, kP2HalfRows,
-                             CU_TENSOR_MAP_SWIZZLE_NONE))
-      return rc;
-    PairParams p{};
+    RoutedParams p{};
+    p.pgroup = routed_pgroup(hidden);
     p.N = static_cast<int>(2 * inter);
+    p.glu_inter = static_cast<int>(inter);
     p.K = static_cast<int>(hidden);
-    p.bn = 256;
-    p.num_m_blocks = cap_blocks;
-    p.num_n_blocks = static_cast<int>((inter + p.bn / 2 - 1) / (p.bn / 2));
+    p.num_wblocks = static_cast<int>((inter + 127) / 128);
     p.w_scales = static_cast<const uint8_t*>(w13_scale);
     p.lds = hidden / 32;
     p.w_rows_per_expert = 2 * inter;
-    p.glu_inter = static_cast<int>(inter);
+    p.chunks = chunks;
+    p.num_chunks = nchunks;
+    p.max_chunks = static_cast<int>(max_chunks);
     p.sorted_ids = rid;
-    p.block_expert = block_expert;
-    p.num_post_padded = post;
     p.num_routes = static_cast<int>(cap);
     p.top_k = 1;
     p.out = hbuf;
     p.ldo = inter;
     p.out_dtype = MXFP4_DTYPE_BF16;
-    p.vec_ok = 1;
-    if (int rc = routed_pair_gemm<A_TMA, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
+    if (int rc = launch_routed<EPI_GLU, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
   }
   {
-    CUtensorMap ta, tb;
-    if (int rc = make_map_2d(&ta, hbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inter, cap, inter * 2, kP2BK,
-                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+    CUtensorMap tw, tx16, tx128;
+    if (int rc = routed_maps(&tw, &tx16, &tx128, w2, static_cast<int64_t>(el) * hidden, inter, hbuf, cap, inter, false,
+                             false))
       return rc;
-    if (int rc = make_map_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inter / 2,
-                             static_cast<uint64_t>(el) * hidden, inter / 2, kP2BK / 2, kP2HalfRows,
-                             CU_TENSOR_MAP_SWIZZLE_NONE))
-      return rc;
-    PairParams p{};
+    RoutedParams p{};
+    p.pgroup = routed_pgroup(inter);
     p.N = static_cast<int>(hidden);
     p.K = static_cast<int>(inter);
-    p.bn = 256;
-    p.num_m_blocks = cap_blocks;
-    p.num_n_blocks = static_cast<int>((hidden + p.bn - 1) / p.bn);
+    p.num_wblocks = static_cast<int>((hidden + 255) / 256);
     p.w_scales = static_cast<const uint8_t*>(w2_scale);
     p.lds = inter / 32;
     p.w_rows_per_expert = hidden;
+    p.chunks = chunks;
+    p.num_chunks = nchunks;
+    p.max_chunks = static_cast<int>(max_chunks);
     p.sorted_ids = rid;
-    p.block_expert = block_expert;
-    p.num_post_padded = post;
     p.num_routes = static_cast<int>(cap);
     p.top_k = 1;
     p.out = yr[rank];
@@ -1436,8 +1509,7 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
     p.mul_w = 1;
     p.c_stride_t = hidden;
     p.c_stride_j = 0;
-    p.vec_ok = 1;
-    if (int rc = routed_pair_gemm<A_TMA, EPI_MOE>(false, ta, tb, p, info.sms, s)) return rc;
+    if (int rc = launch_routed<EPI_MOE, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
   }
   peer_barrier_kernel<<<1, 32, 0, s>>>(pf, rank, world, counter);
   MX_CUDA(cudaGetLastError());

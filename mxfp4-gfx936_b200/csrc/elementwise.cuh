@@ -177,11 +177,16 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
 
 constexpr int kOffsetsTileInts = 9216;  // 36 KB of counts per tile
 
+// Optional route chunks for the routed GEMMs (rt_chunks != nullptr): every
+// expert's padded rows are cut into chunks of at most chunk_blocks blocks;
+// chunk i of the table is int4 {first row, rows, expert, 0}, in expert order,
+// and rt_num_chunks[0] holds their number.
 __global__ void __launch_bounds__(1024) route_offsets_kernel(
     int32_t* __restrict__ hist, int num_chunks, int num_experts, int block_m, int64_t num_routes,
     int32_t* __restrict__ blk_off, int32_t* __restrict__ sorted_ids,
     int32_t* __restrict__ block_expert, int32_t* __restrict__ num_post_padded,
-    int64_t capacity_blocks) {
+    int64_t capacity_blocks, int4* __restrict__ rt_chunks = nullptr, int32_t* __restrict__ rt_num_chunks = nullptr,
+    int chunk_blocks = 1) {
   __shared__ int32_t tile[kOffsetsTileInts];
   __shared__ int32_t total_s[kMaxExperts];
   __shared__ int32_t scan_s[kMaxExperts];
@@ -249,6 +254,29 @@ __global__ void __launch_bounds__(1024) route_offsets_kernel(
     for (int b = lane; b < nbx; b += 32) block_expert[first + b] = x;
     const int64_t base = static_cast<int64_t>(first) * block_m;
     for (int i = cnt + lane; i < nbx * block_m; i += 32) sorted_ids[base + i] = pad;
+  }
+  if (rt_chunks == nullptr) return;
+  // chunk table: exclusive scan of the per-expert chunk counts (one expert per thread)
+  __syncthreads();
+  const int nc = e < num_experts ? (nb + chunk_blocks - 1) / chunk_blocks : 0;
+  int chunks_total;
+  const int cexcl_in_warp = warp_excl_scan(nc, lane, chunks_total);
+  if (lane == 0) warp_sums[wid] = chunks_total;
+  __syncthreads();
+  if (wid == 0) {
+    int t;
+    const int ex = warp_excl_scan(warp_sums[lane], lane, t);
+    warp_sums[lane] = ex;
+    if (lane == 0) rt_num_chunks[0] = t;
+  }
+  __syncthreads();
+  if (e < num_experts) {
+    const int c0 = cexcl_in_warp + warp_sums[wid];
+    for (int i = 0; i < nc; ++i) {
+      const int b0 = i * chunk_blocks;
+      const int nbl = min(chunk_blocks, nb - b0);
+      rt_chunks[c0 + i] = make_int4((excl + b0) * block_m, nbl * block_m, e, 0);
+    }
   }
 }
 

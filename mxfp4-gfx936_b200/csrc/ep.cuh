@@ -4,15 +4,16 @@
 // mapped into every other rank (CUDA IPC), so these kernels read and write
 // peers' memory directly over NVLink:
 //   counts[G][E]   route counts: row s written by rank s into every rank
-//   xr[cap, H]     owner's activations in routed order (256-row blocks per
-//                  local expert, padded), written by the sources' dispatch
+//   xr[cap, H]     owner's activations in routed order (every local expert
+//                  padded to 32 rows), written by the sources' dispatch
 //   wr[cap]        route weight of each xr row (FP32)
 //   yr[cap, H]     owner's weighted down-projection rows, read back by the
 //                  sources' combine
 // Layer: count -> barrier -> plan (every rank derives every owner's block
 // layout from the same count matrix) + stable local routing -> dispatch
 // (push rows into the owners' xr) -> barrier -> gate_up and down GEMMs on the
-// owner (the single-GPU kernels, one route per row) -> barrier -> combine
+// owner (the single-GPU routed kernels over the plan's route chunks, one
+// route per row) -> barrier -> combine
 // (pull the top_k rows of each token, FP32 sum in slot order: the single-GPU
 // combine's order, so the result is bit-identical to the single-GPU layer).
 #pragma once
@@ -23,7 +24,8 @@
 namespace mx {
 
 constexpr int kEpMaxRanks = 8;
-constexpr int kEpBlock = 256;  // routed rows per GEMM block (the pair kernel's M)
+constexpr int kEpBlock = 32;   // padding granularity of every local expert's rows (the routed GEMMs' block)
+constexpr int kEpChunkBlocks = 8;  // a route chunk: at most 8 blocks (256 rows, the routed GEMMs' N)
 
 struct EpPeers {
   void* p[kEpMaxRanks];
@@ -95,7 +97,8 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t* __restrict
                                                        int rank, int32_t* __restrict__ send_base,
                                                        int32_t* __restrict__ lstart, int32_t* __restrict__ block_expert,
                                                        int32_t* __restrict__ num_post_padded, int32_t* __restrict__ rid,
-                                                       int cap, int cap_blocks) {
+                                                       int cap, int cap_blocks, int4* __restrict__ chunks,
+                                                       int32_t* __restrict__ num_chunks) {
   __shared__ int warp_tmp[33];
   __shared__ int scan_nb[kMaxExperts];
   __shared__ int nb_s[kMaxExperts];
@@ -139,6 +142,22 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t* __restrict
     for (int b = lane; b < nb_s[g]; b += 32) block_expert[bstart + b] = x;
     const int base = bstart * kEpBlock;
     for (int i = lane; i < nb_s[g] * kEpBlock; i += 32) rid[base + i] = i < tot_s[g] ? base + i : cap;
+  }
+  // route chunks of the owner's experts for the routed GEMMs: {first row,
+  // rows, local expert, 0}, at most kEpChunkBlocks blocks each
+  __syncthreads();
+  const bool mine = e >= e0 && e < e0 + el;
+  const int nc = mine ? (nb + kEpChunkBlocks - 1) / kEpChunkBlocks : 0;
+  int t_nc;
+  const int cb = block_excl_scan_1024(nc, warp_tmp, t_nc);
+  if (threadIdx.x == 0) num_chunks[0] = t_nc;
+  if (mine) {
+    const int bstart = scan_nb[e] - scan_nb[e0];
+    for (int i = 0; i < nc; ++i) {
+      const int b0 = i * kEpChunkBlocks;
+      const int nbl = min(kEpChunkBlocks, nb - b0);
+      chunks[cb + i] = make_int4((bstart + b0) * kEpBlock, nbl * kEpBlock, e - e0, 0);
+    }
   }
 }
 

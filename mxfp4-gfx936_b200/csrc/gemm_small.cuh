@@ -273,6 +273,298 @@ __global__ void __launch_bounds__(BMODE == B_DECODE ? 256 + 32 * kSmDecodeWarps 
   if (warp == 1) tmem_dealloc(tmem_base, tmem_cols);
 }
 
+// ---------------------------------------------------------------------------
+// Fused few-token linear with the decoded weights in tensor memory.
+//
+// Same tiling, K split, MMA sequence and reduction as mxfp4_linear_small_kernel
+// (so its results are the safe mode's bits), but the decoded weight tile never
+// touches shared memory: decoder warps turn the packed codes they read from
+// shared memory into BF16/FP16 pairs in registers and store them with
+// tcgen05.st into a ring of tensor-memory slots (one lane per weight row, 32
+// columns per 64-K stage), and the MMA reads operand A from there.  Three
+// independent rings:
+//   packed  [kTmPSlots]  TMA -> decoders; a slot is free once every decoder
+//                        warp has read its words (before the MMA), so the
+//                        producer runs up to kTmPSlots stages ahead;
+//   x       [kTmXSlots]  TMA -> MMA (operand B), freed by the MMA's commit;
+//   A       [kTmASlots]  decoders -> MMA in tensor memory, freed by commit.
+// With 64-K stages and at most a few tens of stages per CTA, the packed ring
+// holds a large part of the CTA's weight bytes in flight at once.
+// ---------------------------------------------------------------------------
+constexpr int kTmPSlots = 4;   // packed ring: each slot holds a group of 4 stages (one TMA load)
+constexpr int kTmPGroup = 4;
+constexpr int kTmPGroupBytes = kSmPBytes * kTmPGroup;  // 128 rows x 4 stages x 32 B
+constexpr int kTmXSlots = 4;
+constexpr int kTmASlots = 8;
+constexpr int kTmDecodeWarps = 16;  // 4 warps per TMEM lane quarter, taking consecutive pairs of stages
+
+__host__ __device__ constexpr int tm_small_acc_cols(int mp) {
+  return mp <= 32 ? 32 : (mp <= 64 ? 64 : (mp <= 128 ? 128 : 256));
+}
+__host__ __device__ constexpr uint32_t tm_small_alloc_cols(int mp) {
+  return tm_small_acc_cols(mp) + kTmASlots * 32 <= 256 ? 256u : 512u;
+}
+
+template <bool FP16>
+__global__ void __launch_bounds__(256 + 32 * kTmDecodeWarps, 1)
+    mxfp4_linear_small_tmem_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                                   const SmallParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int x_bytes = p.mp * 128;
+  // [x ring][packed ring]; the partial tile reuses the start after the main loop
+  const int x_off = 0;
+  const int p_off = kTmXSlots * x_bytes;
+  const int data_bytes = p_off + kTmPSlots * kTmPGroupBytes;
+  const int part_bytes = kSmRows * p.mp * 4;
+  const int bar_off = ((data_bytes > part_bytes ? data_bytes : part_bytes) + 15) & ~15;
+  uint64_t* pfull = reinterpret_cast<uint64_t*>(smem + bar_off);
+  uint64_t* pempty = pfull + kTmPSlots;
+  uint64_t* xfull = pempty + kTmPSlots;
+  uint64_t* xempty = xfull + kTmXSlots;
+  uint64_t* aready = xempty + kTmXSlots;
+  uint64_t* aempty = aready + kTmASlots;
+  uint64_t* tfull = aempty + kTmASlots;
+  uint64_t* drain = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* part = reinterpret_cast<float*>(smem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank_sm();
+  const int n0 = blockIdx.y * kSmRows;
+  const int KT = p.K / kSmBK;
+  const int kt0 = static_cast<int>((static_cast<int64_t>(KT) * rank) / p.ks);
+  const int kt1 = static_cast<int>((static_cast<int64_t>(KT) * (rank + 1)) / p.ks);
+  const int nst = kt1 - kt0;
+  const int acc_cols = tm_small_acc_cols(p.mp);
+  const uint32_t alloc_cols = tm_small_alloc_cols(p.mp);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTmPSlots; ++s) {
+      mbar_init(&pfull[s], 1);
+      mbar_init(&pempty[s], 2 * kTmPGroup);  // a pair's decoder warp of each lane quarter, 2 pairs per group
+    }
+    for (int s = 0; s < kTmXSlots; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int s = 0; s < kTmASlots; ++s) {
+      mbar_init(&aready[s], 4);
+      mbar_init(&aempty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, alloc_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_a = tmem_base + acc_cols;  // A slot i at columns [acc_cols + 32 i, +32)
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- packed-weight producer
+    // one TMA load per group of 4 stages (128 rows x 128 B)
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      uint32_t armed = 0, armed_par = 0;
+      bool ok = true;
+      for (int gi = 0; gi * kTmPGroup < nst; ++gi) {
+        const int s = gi % kTmPSlots;
+        const uint32_t ph = (gi / kTmPSlots) & 1;
+        if (!mbar_wait(&pempty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&pfull[s], kTmPGroupBytes);
+        armed |= 1u << s;
+        armed_par = (armed_par & ~(1u << s)) | (ph << s);
+        tma_load_2d_hint(smem + p_off + s * kTmPGroupBytes, &tmap_w, &pfull[s], (kt0 + gi * kTmPGroup) * (kSmBK / 2),
+                         n0, pol_w);
+      }
+      if (!ok || *abort_flag)
+        for (int s = 0; s < kTmPSlots; ++s)
+          if (armed & (1u << s)) mbar_drain(&pfull[s], (armed_par >> s) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 2 || warp == 3) {
+    // ---------------------------------------------------------- activation producers
+    // warp 2 takes the even stages, warp 3 the odd ones (two issuing threads)
+    if (lane == 0) {
+      const int par = warp - 2;
+      uint32_t armed = 0, armed_par = 0;
+      bool ok = true;
+      for (int it = par; it < nst; it += 2) {
+        const int s = it % kTmXSlots;
+        const uint32_t ph = (it / kTmXSlots) & 1;
+        if (!mbar_wait(&xempty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&xfull[s], x_bytes);
+        armed |= 1u << s;
+        armed_par = (armed_par & ~(1u << s)) | (ph << s);
+        tma_load_2d(smem + x_off + s * x_bytes, &tmap_x, &xfull[s], (kt0 + it) * kSmBK, 0);
+      }
+      if (!ok || *abort_flag)
+        for (int s = 0; s < kTmXSlots; ++s)
+          if (armed & (1u << s)) mbar_drain(&xfull[s], (armed_par >> s) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(FP16 ? 0 : 1, kSmRows, p.mp);
+      bool ok = true, issued = false;
+      for (int it = 0; it < nst; ++it) {
+        const int sa = it % kTmASlots, sx = it % kTmXSlots;
+        if (!mbar_wait(&aready[sa], (it / kTmASlots) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&xfull[sx], (it / kTmXSlots) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t bdesc = desc_sw128(smem_u32(smem + x_off + sx * x_bytes));  // x: MMA B (N = mp)
+        const uint32_t a_slot = tmem_a + sa * 32;
+#pragma unroll
+        for (int k = 0; k < kSmBK / 16; ++k) umma_f16_ta(tmem_base, a_slot + 8 * k, bdesc + 2 * k, idesc, (it | k) != 0);
+        umma_commit(&aempty[sa]);
+        umma_commit(&xempty[sx]);
+        issued = true;
+      }
+      if (ok) umma_commit(tfull);
+      else if (issued) {
+        umma_commit(drain);
+        mbar_drain(drain, 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------- decoders -> tensor memory
+    // warp 8 + dw: lane quarter q = dw % 4 (= warp % 4, the quarter it may
+    // address) and group g = dw / 4.  Stages go to the quarter's four warps in
+    // pairs (pair m = stages 2m, 2m + 1 to the warp with m % 4 == g), each
+    // decoding both 64-K stages of its 32 rows into two 32-column A slots, so
+    // eight stages are in flight per quarter.
+    const int dw = warp - 8;
+    const int q = dw & 3, g = dw >> 2;
+    const int r = q * 32 + lane;  // weight row of the tile = TMEM lane
+    const int grow = n0 + r;
+    const bool valid = grow < p.N;
+    const uint8_t* srow = p.w_scales + (valid ? static_cast<int64_t>(grow) * p.lds : 0);
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    for (int it0 = 2 * g; it0 < nst; it0 += 8) {
+      int nb = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int it = it0 + h;
+        if (it >= nst) break;
+        const int kt = kt0 + it;
+        const int gi = it / kTmPGroup;  // packed group (both stages of a pair share it)
+        const int sp = gi % kTmPSlots, sa = it % kTmASlots;
+        const uint32_t sc = valid ? static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(srow + 2 * kt)) : 0x7F7Fu;
+        // warp-uniform waits: the tcgen05.st / wait::st below are .sync.aligned
+        if (h == 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&pfull[sp], (gi / kTmPSlots) & 1, abort_flag))) { nb = -1; break; }
+        const uint32_t prow = smem_u32(smem + p_off + sp * kTmPGroupBytes) + r * 32 * kTmPGroup + (it % kTmPGroup) * 32;
+        const uint4 q0 = ld_shared_v4(prow);
+        const uint4 q1 = ld_shared_v4(prow + 16);
+        const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        uint32_t v[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t code = (sc >> (8 * (i >> 2))) & 0xFF;  // words 0-3: first 32 K, 4-7: second
+          uint4 d;
+          if (FP16) d = decode8_f16(words[i], e8m0_to_f32(code));
+          else d = decode8_bf16(words[i], e8m0_to_bf16x2(code));
+          v[4 * i] = d.x;
+          v[4 * i + 1] = d.y;
+          v[4 * i + 2] = d.z;
+          v[4 * i + 3] = d.w;
+        }
+        // after the pair's last words are used, the packed slot may be refilled
+        if (h == 1 || it + 1 >= nst) {
+          asm volatile("" ::"r"(v[0]), "r"(v[31]));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[sp]);
+        }
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&aempty[sa], ((it / kTmASlots) & 1) ^ 1, abort_flag))) { nb = -1; break; }
+        tc_fence_after();
+        tmem_st_32x32b_x32(tmem_a + lane_base + sa * 32, v);
+        ++nb;
+      }
+      if (nb < 0) break;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0)
+        for (int h = 0; h < nb; ++h) mbar_arrive(&aready[(it0 + h) % kTmASlots]);
+    }
+  }
+
+  // ---------------------------------------------------------------- partials
+  if (warp >= 4 && warp < 8) {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    if (nst > 0 && mbar_wait(tfull, 0, abort_flag)) {
+      tc_fence_after();
+      for (int cc = 0; cc < p.mp / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cc * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) part[(cc * 32 + i) * kSmRows + row] = __uint_as_float(v[i]);
+      }
+    } else {
+      for (int c = 0; c < p.mp; ++c) part[c * kSmRows + row] = 0.0f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_sm();  // every CTA's partial tile is in its shared memory
+  tc_fence_after();
+
+  // ---------------------------------------------------------------- reduction (as mxfp4_linear_small_kernel)
+  {
+    const int rows_per = ((kSmRows + p.ks - 1) / p.ks + 3) & ~3;
+    const int r_beg = static_cast<int>(rank) * rows_per;
+    const int r_end = min(kSmRows, r_beg + rows_per);
+    const int quads = r_end > r_beg ? (r_end - r_beg) / 4 : 0;
+    const int esz = p.out_dtype == MXFP4_DTYPE_F32 ? 4 : 2;
+    const uint32_t part_local = smem_u32(part);
+    for (int i = threadIdx.x; i < quads * p.M; i += blockDim.x) {
+      const int rr = r_beg + 4 * (i % quads);
+      const int tok = i / quads;
+      const uint32_t off = static_cast<uint32_t>((tok * kSmRows + rr) * 4);
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int c = 0; c < p.ks; ++c) {
+        const float4 v = ld_dsmem_v4(mapa_sm(part_local + off, c));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = n0 + rr + j;
+        if (col >= p.N) continue;
+        float v = round_to(a4[j], p.out_dtype);
+        if (p.bias != nullptr) v = round_to(v + load_weight(p.bias, p.out_dtype, col), p.out_dtype);
+        uint8_t* o = static_cast<uint8_t*>(p.out) + (static_cast<int64_t>(tok) * p.ldo + col) * esz;
+        if (p.out_dtype == MXFP4_DTYPE_F32) *reinterpret_cast<float*>(o) = v;
+        else if (p.out_dtype == MXFP4_DTYPE_BF16) *reinterpret_cast<__nv_bfloat16*>(o) = __float2bfloat16_rn(v);
+        else *reinterpret_cast<__half*>(o) = __float2half_rn(v);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_sm();  // peers finished reading this CTA's partials
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, alloc_cols);
+}
+
 }  // namespace mx
 
 namespace mx {

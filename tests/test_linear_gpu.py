@@ -47,6 +47,7 @@ def test_matches_reference_golden(monkeypatch, backend, case):
 
 
 SHAPES = [(1, 64, 128), (2, 99, 256), (1, 5120, 2048), (2, 96, 8192), (8, 64, 128), (16, 256, 2048), (16, 128, 24576), (64, 5120, 2048), (130, 384, 256),
+          (40, 384, 16384),  # 32 stages per CTA: the few-token kernel's packed ring wraps
           (370, 512, 2048), (300, 1000, 512), (257, 2048, 4096),
           # four-CTA kernel (>= 4 row blocks of 256): odd row-block count, ragged N, K shorter than the ring
           (1100, 1000, 512), (1024, 640, 1024), (2048, 2048, 256)]
