@@ -363,9 +363,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
     if (leader && lane == 0) {
       int it = 0, tl = 0;
       bool ok = true, issued = false;
+      // the next tile's route count is read one tile ahead (it sets the MMA's N)
+      int n_next = cluster_id < num_tiles ? p.chunks[cluster_id / p.num_wblocks].y : 0;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++tl) {
-        const int4 ch = p.chunks[t / p.num_wblocks];
-        const uint32_t idesc = idesc_f16(FP16 ? 0 : 1, kP2BM, ch.y);
+        const int n_tile = n_next;
+        if (t + num_clusters < num_tiles) n_next = p.chunks[(t + num_clusters) / p.num_wblocks].y;
+        const uint32_t idesc = idesc_f16(FP16 ? 0 : 1, kP2BM, n_tile);
         if (!mbar_wait_cluster(tempty, (tl & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt, ++it) {
@@ -403,27 +406,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t ready_leader = mapa_shared(smem_u32(ready), 0);
     const int total = num_tiles > cluster_id ? ((num_tiles - 1 - cluster_id) / num_clusters + 1) * KT : 0;
-    int tile_seq = -1;
-    const uint8_t* srow = p.w_scales;
-    bool valid = false;
+    // The scale codes of a pair (2 stages x 2 blocks of 32 K) are one aligned
+    // 32-bit word of the row's scales (K is a multiple of 128).  Each pair's
+    // word is loaded while the previous pair is decoded, so the load latency
+    // is off the critical path; the chunk table is read only when the next
+    // pair starts another tile.
+    int next_tile = -1;
+    const uint8_t* next_srow = p.w_scales;
+    bool next_valid = false;
+    auto scale_word = [&](int it) -> uint32_t {
+      if (it >= total) return 0x7F7F7F7Fu;
+      const int ts = it / KT, kt = it % KT;
+      if (ts != next_tile) {
+        next_tile = ts;
+        const int t = cluster_id + ts * num_clusters;
+        const int4 ch = p.chunks[t / p.num_wblocks];
+        const int64_t grow = rt_weight_row<EPI>(p, ch.z, t % p.num_wblocks, rank, r, next_valid);
+        next_srow = p.w_scales + (next_valid ? grow * p.lds : 0);
+      }
+      return next_valid ? ldg_nc_u32(next_srow + 2 * (kt % KTw)) : 0x7F7F7F7Fu;
+    };
+    uint32_t sc_next = scale_word(2 * g);
     for (int it0 = 2 * g; it0 < total; it0 += 8) {
+      const uint32_t sc_pair = sc_next;
+      sc_next = scale_word(it0 + 8);
       int nb = 0;  // stages of this pair (KT is even: the pair never straddles a tile)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int it = it0 + h;
         if (it >= total) break;
-        const int ts = it / KT, kt = it % KT;
-        if (ts != tile_seq) {
-          tile_seq = ts;
-          const int t = cluster_id + ts * num_clusters;
-          const int4 ch = p.chunks[t / p.num_wblocks];
-          const int64_t grow = rt_weight_row<EPI>(p, ch.z, t % p.num_wblocks, rank, r, valid);
-          srow = p.w_scales + (valid ? grow * p.lds : 0);
-        }
         const int gi = it / p.pgroup;  // packed group of this stage (both stages of a pair share it)
         const int sp = gi % kRtPSlots, a = it % kRtASlots;
-        const uint32_t sc = valid ? static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(srow + 2 * (kt % KTw)))
-                                  : 0x7F7Fu;
+        const uint32_t sc = sc_pair >> (16 * h);
         // warp-uniform waits: the tcgen05.st / wait::st below are .sync.aligned
         if (h == 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&pfull[sp], (gi / kRtPSlots) & 1, abort_flag))) { nb = -1; break; }
         const uint32_t prow = smem_u32(smem + kRtOffP + sp * kRtPBytes) + r * 32 * p.pgroup + (it % p.pgroup) * 32;

@@ -454,16 +454,28 @@ __global__ void __launch_bounds__(256 + 32 * kTmDecodeWarps, 1)
     const bool valid = grow < p.N;
     const uint8_t* srow = p.w_scales + (valid ? static_cast<int64_t>(grow) * p.lds : 0);
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    // a pair's four scale codes are one aligned 32-bit word when the pair
+    // starts at an even global stage; its load overlaps the previous pair
+    auto scale_word = [&](int it) -> uint32_t {
+      if (!valid || it >= nst) return 0x7F7F7F7Fu;
+      const int kt = kt0 + it;
+      if ((kt & 1) == 0) return ldg_nc_u32(srow + 2 * kt);
+      const uint32_t lo = *reinterpret_cast<const uint16_t*>(srow + 2 * kt);
+      const uint32_t hi = it + 1 < nst ? *reinterpret_cast<const uint16_t*>(srow + 2 * kt + 2) : 0x7F7Fu;
+      return lo | (hi << 16);
+    };
+    uint32_t sc_next = scale_word(2 * g);
     for (int it0 = 2 * g; it0 < nst; it0 += 8) {
+      const uint32_t sc_pair = sc_next;
+      sc_next = scale_word(it0 + 8);
       int nb = 0;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int it = it0 + h;
         if (it >= nst) break;
-        const int kt = kt0 + it;
         const int gi = it / kTmPGroup;  // packed group (both stages of a pair share it)
         const int sp = gi % kTmPSlots, sa = it % kTmASlots;
-        const uint32_t sc = valid ? static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(srow + 2 * kt)) : 0x7F7Fu;
+        const uint32_t sc = sc_pair >> (16 * h);
         // warp-uniform waits: the tcgen05.st / wait::st below are .sync.aligned
         if (h == 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&pfull[sp], (gi / kTmPSlots) & 1, abort_flag))) { nb = -1; break; }
         const uint32_t prow = smem_u32(smem + p_off + sp * kTmPGroupBytes) + r * 32 * kTmPGroup + (it % kTmPGroup) * 32;

@@ -58,3 +58,17 @@ def same_bits(a, b):
     b = np.asarray(b, dtype=np.float32)
     nan = np.isnan(a) & np.isnan(b)
     return bool(np.all((a.view(np.uint32) == b.view(np.uint32)) | nan))
+
+
+def vllm_adapter(name="mxfp4_vllm_adapter"):
+    """The package's vLLM adapter module.  Importing it sets
+    ``MXFP4_GFX936_BACKEND`` from ``MXFP4_IMPLEMENTATION`` (as the reference
+    adapter does); the variable is put back so other tests see their own."""
+    saved = os.environ.get("MXFP4_GFX936_BACKEND")
+    try:
+        return load_by_path(name, PKG / "vllm_adapter.py")
+    finally:
+        if saved is None:
+            os.environ.pop("MXFP4_GFX936_BACKEND", None)
+        else:
+            os.environ["MXFP4_GFX936_BACKEND"] = saved

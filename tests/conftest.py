@@ -16,3 +16,17 @@ if str(ROOT / "tests") not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 GPU and the built CUDA library")
+
+
+@pytest.fixture(scope="session")
+def ct_checkpoint_dir(tmp_path_factory):
+    """A small compressed-tensors MXFP4 checkpoint written by compressed-tensors
+    itself (``tests/golden/make_ct_checkpoint.py``)."""
+    import os
+    import subprocess
+
+    out = tmp_path_factory.mktemp("ct_checkpoint")
+    env = dict(os.environ, TORCHDYNAMO_DISABLE="1")
+    subprocess.run([sys.executable, str(ROOT / "tests" / "golden" / "make_ct_checkpoint.py"), str(out)],
+                   check=True, env=env, timeout=900)
+    return out
