@@ -400,7 +400,7 @@ int routed_maps(CUtensorMap* tw, CUtensorMap* tx16, CUtensorMap* tx128, const vo
   const CUtensorMapDataType xt = fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const uint32_t box_bytes = static_cast<uint32_t>(routed_pgroup(kw) * (kP2BK / 2));
   if (int rc = make_map_2d(tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, kw / 2, rows_total, kw / 2, box_bytes,
-                           glu ? 64 : 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+                           glu ? 64 : 128, box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
     return rc;
   const uint64_t rows = static_cast<uint64_t>(std::max<int64_t>(cap, 1));
   if (int rc = make_map_2d(tx16, xr, xt, 2, ka, rows, ka * 2, kP2BK, 16, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
@@ -658,7 +658,7 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
     if (int rc = make_map_2d(&ta, x, xt, 2, k, m, ldx * 2, kSmBK, q.mp, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
     if (mode == MXFP4_LINEAR_FUSED && wd == nullptr) {
       if (int rc = make_map_2d(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, n, ldw,
-                               kTmPGroup * (kSmBK / 2), kSmRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+                               kTmPGroup * (kSmBK / 2), kSmRows, CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
       if (fp16) return push(launch_small_tmem<true>(ta, tb, q, s));
       return push(launch_small_tmem<false>(ta, tb, q, s));
@@ -985,6 +985,73 @@ MoeCompute moe_compute(int a_dtype, int c_dtype) {
   return {MXFP4_DTYPE_BF16, 1};
 }
 
+// Which grouped GEMM a routed call runs on.  While experts receive few routes
+// the tensor-memory decoder kernel (gemm_routed.cuh: 32-route padding, each
+// expert's weights decoded once per chunk of up to 256 routes) wins; once the
+// average expert receives kPairRoutesPerExpert routes the CTA-pair kernel over
+// 256-route blocks (gemm2.cuh: shared-memory decode, two accumulators, the
+// epilogue of one tile under the main loop of the next) is faster.  Both give
+// the same bits: every output is the same single FP32 dot product of the same
+// BF16 operands, rounded by the same epilogue chain.
+constexpr int64_t kPairRoutesPerExpert = 128;
+bool moe_pair_path(int64_t routes, int num_experts) {
+  return routes >= kPairRoutesPerExpert * static_cast<int64_t>(num_experts);
+}
+
+// Routing of the pair path: 256-route blocks, no chunk table.
+struct PairRouting {
+  int64_t cap;
+  int32_t* sorted;
+  int32_t* block_expert;
+  int32_t* post;
+  uint8_t* route_ws;
+};
+
+size_t pair_routing_bytes(int64_t routes, int num_experts) {
+  const int64_t cap = route_capacity(routes, num_experts, kP2BM);
+  return align_up(sizeof(int32_t) * std::max<int64_t>(cap, 1), 256) + align_up(sizeof(int32_t) * (cap / kP2BM + 1), 256) +
+         256 + route_ws_bytes(routes, num_experts);
+}
+
+PairRouting carve_pair_routing(uint8_t*& ws, int64_t routes, int num_experts) {
+  PairRouting r;
+  r.cap = route_capacity(routes, num_experts, kP2BM);
+  r.sorted = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * std::max<int64_t>(r.cap, 1), 256);
+  r.block_expert = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(sizeof(int32_t) * (r.cap / kP2BM + 1), 256);
+  r.post = reinterpret_cast<int32_t*>(ws);
+  ws += 256;
+  r.route_ws = ws;
+  ws += route_ws_bytes(routes, num_experts);
+  return r;
+}
+
+// A converted to the operand dtype of the routed op (dequantised packed MXFP4,
+// split BF16 parts, or a cast) into dst, or A itself.
+int convert_activations(const void* A, int a_dtype, const void* a_mx_scale, const MoeCompute& mc, int64_t num_tokens,
+                        int64_t k, void* dst, const DevInfo& info, cudaStream_t s, void* stream, const void*& a_eff) {
+  a_eff = A;
+  const int cdt = mc.dtype;
+  if (a_dtype == MXFP4_DTYPE_U8) {
+    if (int rc = mxfp4_dequant(A, a_mx_scale, dst, cdt, num_tokens, k, stream)) return rc;
+    a_eff = dst;
+  } else if (mc.parts > 1) {
+    const int64_t cnt = num_tokens * k;
+    const int grid = static_cast<int>(std::min<int64_t>((cnt + 255) / 256, int64_t(info.sms) * 8));
+    split_bf16_kernel<<<grid, 256, 0, s>>>(A, a_dtype, num_tokens, k, mc.parts, reinterpret_cast<__nv_bfloat16*>(dst));
+    MX_CUDA(cudaGetLastError());
+    a_eff = dst;
+  } else if (a_dtype != cdt) {
+    const int64_t cnt = num_tokens * k;
+    const int grid = static_cast<int>(std::min<int64_t>((cnt + 255) / 256, int64_t(info.sms) * 8));
+    cast_kernel<<<grid, 256, 0, s>>>(A, a_dtype, dst, cdt, cnt);
+    MX_CUDA(cudaGetLastError());
+    a_eff = dst;
+  }
+  return MXFP4_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -995,10 +1062,11 @@ size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_exp
                                       int64_t k, int a_dtype, int c_dtype) {
   (void)n;
   const int64_t routes = num_tokens * top_k;
-  const int64_t cap = route_capacity(routes, num_experts, kRtBlock);
+  const bool pair = moe_pair_path(routes, num_experts);
+  const int64_t cap = route_capacity(routes, num_experts, pair ? kP2BM : kRtBlock);
   const MoeCompute mc = moe_compute(a_dtype, c_dtype);
   const int64_t ka = k * mc.parts;  // columns of the converted activations
-  size_t b = rt_routing_bytes(routes, num_experts);
+  size_t b = pair ? pair_routing_bytes(routes, num_experts) : rt_routing_bytes(routes, num_experts);
   if (a_dtype != mc.dtype || mc.parts > 1) b += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
   b += align_up(static_cast<size_t>(std::max<int64_t>(cap, 1)) * ka * 2, 256);  // activations in routed order
   return b;
@@ -1041,24 +1109,58 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   MX_CUDA(cudaMemsetAsync(C, 0, static_cast<size_t>(routes) * n * esz, s));
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  const RtRouting rt = carve_rt_routing(ws, routes, num_experts);
-  const void* a_eff = A;
-  if (a_dtype == MXFP4_DTYPE_U8) {
-    if (int rc = mxfp4_dequant(A, a_mx_scale, ws, cdt, num_tokens, k, stream)) return rc;
-    a_eff = ws;
-  } else if (mc.parts > 1) {
-    const int64_t cnt = num_tokens * k;
-    const int grid = static_cast<int>(std::min<int64_t>((cnt + 255) / 256, int64_t(info.sms) * 8));
-    split_bf16_kernel<<<grid, 256, 0, s>>>(A, a_dtype, num_tokens, k, mc.parts, reinterpret_cast<__nv_bfloat16*>(ws));
-    MX_CUDA(cudaGetLastError());
-    a_eff = ws;
-  } else if (a_dtype != cdt) {
-    const int64_t cnt = num_tokens * k;
-    const int grid = static_cast<int>(std::min<int64_t>((cnt + 255) / 256, int64_t(info.sms) * 8));
-    cast_kernel<<<grid, 256, 0, s>>>(A, a_dtype, ws, cdt, cnt);
-    MX_CUDA(cudaGetLastError());
-    a_eff = ws;
+  if (moe_pair_path(routes, num_experts)) {
+    // many routes per expert: the pair kernel over 256-route blocks
+    const PairRouting pr = carve_pair_routing(ws, routes, num_experts);
+    const void* a_eff;
+    if (int rc = convert_activations(A, a_dtype, a_mx_scale, mc, num_tokens, k, ws, info, s, stream, a_eff)) return rc;
+    if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kP2BM, pr.sorted, pr.block_expert, pr.post,
+                           pr.cap, pr.route_ws, s))
+      return rc;
+    MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
+    if (a_eff != A) ws += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
+    void* a_routed = ws;
+    if (int rc = run_gather(a_eff, ka, pr.sorted, pr.post, routes, top_k, a_routed, pr.cap, info.sms, s)) return rc;
+    CUtensorMap ta, tb;
+    const CUtensorMapDataType at =
+        cdt == MXFP4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    if (int rc = make_map_2d(&ta, a_routed, at, 2, ka, pr.cap, ka * 2, kP2BK, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k / 2, static_cast<uint64_t>(num_experts) * n,
+                             k / 2, kP2BK / 2, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    PairParams p{};
+    p.N = static_cast<int>(n);
+    p.K = static_cast<int>(ka);
+    p.k_rep = mc.parts;
+    p.bn = 256;
+    p.num_m_blocks = static_cast<int>(pr.cap / kP2BM);
+    p.num_n_blocks = static_cast<int>((n + p.bn - 1) / p.bn);
+    p.a_ptr = static_cast<const uint8_t*>(a_eff);
+    p.lda = ka;
+    p.w_scales = static_cast<const uint8_t*>(B_mx_scale);
+    p.lds = k / 32;
+    p.w_rows_per_expert = n;
+    p.sorted_ids = pr.sorted;
+    p.block_expert = pr.block_expert;
+    p.num_post_padded = pr.post;
+    p.num_routes = static_cast<int>(routes);
+    p.top_k = top_k;
+    p.out = C;
+    p.out_dtype = c_dtype;
+    p.a_scale = a_scale;
+    p.b_scale = b_scale;
+    p.topk_w = topk_weights;
+    p.w_dtype = w_dtype;
+    p.mul_w = mul_routed_weight ? 1 : 0;
+    p.c_stride_t = static_cast<int64_t>(top_k) * n;
+    p.c_stride_j = n;
+    p.vec_ok = aligned(C, 16) && (n * esz) % 16 == 0;
+    return routed_pair_gemm<A_TMA, EPI_MOE>(cdt == MXFP4_DTYPE_F16, ta, tb, p, info.sms, s);
   }
+  const RtRouting rt = carve_rt_routing(ws, routes, num_experts);
+  const void* a_eff;
+  if (int rc = convert_activations(A, a_dtype, a_mx_scale, mc, num_tokens, k, ws, info, s, stream, a_eff)) return rc;
   if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
   MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
   if (a_eff != A) ws += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
@@ -1229,8 +1331,9 @@ int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const vo
 size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t hidden,
                                       int64_t inter) {
   const int64_t routes = num_tokens * top_k;
-  const int64_t cap = std::max<int64_t>(route_capacity(routes, num_experts, kRtBlock), 1);
-  size_t b = rt_routing_bytes(routes, num_experts);
+  const bool pair = moe_pair_path(routes, num_experts);
+  const int64_t cap = std::max<int64_t>(route_capacity(routes, num_experts, pair ? kP2BM : kRtBlock), 1);
+  size_t b = pair ? pair_routing_bytes(routes, num_experts) : rt_routing_bytes(routes, num_experts);
   b += align_up(static_cast<size_t>(cap) * inter * 2, 256);                           // h in routed order
   b += align_up(static_cast<size_t>(std::max<int64_t>(routes, 1)) * hidden * 2, 256);  // weighted down rows
   b += align_up(static_cast<size_t>(cap) * hidden * 2, 256);                          // x in routed order
@@ -1259,71 +1362,154 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   const int64_t routes = num_tokens * top_k;
   if (num_tokens == 0) return MXFP4_OK;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  const RtRouting rt = carve_rt_routing(ws, routes, num_experts);
-  const int64_t cap = std::max<int64_t>(rt.cap, 1);
-  void* hbuf = ws;
-  ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
-  void* ybuf = ws;
-  ws += align_up(static_cast<size_t>(routes) * hidden * 2, 256);
-  void* xbuf = ws;
-
-  if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
-  if (int rc = run_gather(x, hidden, rt.sorted, rt.post, routes, top_k, xbuf, rt.cap, info.sms, s)) return rc;
-
-  // gate_up with fused SiLU(gate) * up -> h [cap, inter] in routed order
-  {
-    CUtensorMap tw, tx16, tx128;
-    if (int rc = routed_maps(&tw, &tx16, &tx128, w13, static_cast<int64_t>(num_experts) * 2 * inter, hidden, xbuf,
-                             cap, hidden, false, true))
+  void* ybuf = nullptr;  // [routes, hidden]: the weighted down rows, by route id
+  if (moe_pair_path(routes, num_experts)) {
+    // many routes per expert: pair kernel over 256-route blocks
+    const PairRouting pr = carve_pair_routing(ws, routes, num_experts);
+    const int64_t cap = std::max<int64_t>(pr.cap, 1);
+    void* hbuf = ws;
+    ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
+    ybuf = ws;
+    ws += align_up(static_cast<size_t>(routes) * hidden * 2, 256);
+    void* xbuf = ws;
+    if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, kP2BM, pr.sorted, pr.block_expert, pr.post,
+                           pr.cap, pr.route_ws, s))
       return rc;
-    RoutedParams p{};
-    p.pgroup = routed_pgroup(hidden);
-    p.N = static_cast<int>(2 * inter);
-    p.glu_inter = static_cast<int>(inter);
-    p.K = static_cast<int>(hidden);
-    p.num_wblocks = static_cast<int>((inter + 127) / 128);
-    p.w_scales = static_cast<const uint8_t*>(w13_scale);
-    p.lds = hidden / 32;
-    p.w_rows_per_expert = 2 * inter;
-    p.chunks = rt.chunks;
-    p.num_chunks = rt.num_chunks;
-    p.max_chunks = static_cast<int>(rt.max_chunks);
-    p.sorted_ids = rt.sorted;
-    p.num_routes = static_cast<int>(routes);
-    p.top_k = top_k;
-    p.out = hbuf;
-    p.ldo = inter;
-    p.out_dtype = MXFP4_DTYPE_BF16;
-    if (int rc = launch_routed<EPI_GLU, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
-  }
-  // down with route weights, scattered to y[route] = [routes, hidden]
-  {
-    CUtensorMap tw, tx16, tx128;
-    if (int rc = routed_maps(&tw, &tx16, &tx128, w2, static_cast<int64_t>(num_experts) * hidden, inter, hbuf, cap,
-                             inter, false, false))
-      return rc;
-    RoutedParams p{};
-    p.pgroup = routed_pgroup(inter);
-    p.N = static_cast<int>(hidden);
-    p.K = static_cast<int>(inter);
-    p.num_wblocks = static_cast<int>((hidden + 255) / 256);
-    p.w_scales = static_cast<const uint8_t*>(w2_scale);
-    p.lds = inter / 32;
-    p.w_rows_per_expert = hidden;
-    p.chunks = rt.chunks;
-    p.num_chunks = rt.num_chunks;
-    p.max_chunks = static_cast<int>(rt.max_chunks);
-    p.sorted_ids = rt.sorted;
-    p.num_routes = static_cast<int>(routes);
-    p.top_k = 1;
-    p.out = ybuf;
-    p.out_dtype = MXFP4_DTYPE_BF16;
-    p.topk_w = topk_weights;
-    p.w_dtype = w_dtype;
-    p.mul_w = 1;
-    p.c_stride_t = hidden;
-    p.c_stride_j = 0;
-    if (int rc = launch_routed<EPI_MOE, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
+    if (int rc = run_gather(x, hidden, pr.sorted, pr.post, routes, top_k, xbuf, pr.cap, info.sms, s)) return rc;
+    // gate_up with fused SiLU(gate) * up -> h [cap, inter] in routed order
+    {
+      CUtensorMap ta, tb;
+      if (int rc = make_map_2d(&ta, xbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hidden, pr.cap, hidden * 2, kP2BK,
+                               kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+      if (int rc = make_map_2d(&tb, w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hidden / 2,
+                               static_cast<uint64_t>(num_experts) * 2 * inter, hidden / 2, kP2BK / 2, kP2HalfRows,
+                               CU_TENSOR_MAP_SWIZZLE_NONE))
+        return rc;
+      PairParams p{};
+      p.N = static_cast<int>(2 * inter);
+      p.K = static_cast<int>(hidden);
+      p.bn = 256;
+      p.num_m_blocks = static_cast<int>(pr.cap / kP2BM);
+      p.num_n_blocks = static_cast<int>((inter + p.bn / 2 - 1) / (p.bn / 2));
+      p.a_ptr = static_cast<const uint8_t*>(x);
+      p.lda = hidden;
+      p.w_scales = static_cast<const uint8_t*>(w13_scale);
+      p.lds = hidden / 32;
+      p.w_rows_per_expert = 2 * inter;
+      p.glu_inter = static_cast<int>(inter);
+      p.sorted_ids = pr.sorted;
+      p.block_expert = pr.block_expert;
+      p.num_post_padded = pr.post;
+      p.num_routes = static_cast<int>(routes);
+      p.top_k = top_k;
+      p.out = hbuf;
+      p.ldo = inter;
+      p.out_dtype = MXFP4_DTYPE_BF16;
+      p.vec_ok = 1;
+      if (int rc = routed_pair_gemm<A_TMA, EPI_GLU>(false, ta, tb, p, info.sms, s)) return rc;
+    }
+    // down with route weights, scattered to y[route]
+    {
+      CUtensorMap ta, tb;
+      if (int rc = make_map_2d(&ta, hbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inter, pr.cap, inter * 2, kP2BK,
+                               kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+      if (int rc = make_map_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inter / 2,
+                               static_cast<uint64_t>(num_experts) * hidden, inter / 2, kP2BK / 2, kP2HalfRows,
+                               CU_TENSOR_MAP_SWIZZLE_NONE))
+        return rc;
+      PairParams p{};
+      p.N = static_cast<int>(hidden);
+      p.K = static_cast<int>(inter);
+      p.bn = 256;
+      p.num_m_blocks = static_cast<int>(pr.cap / kP2BM);
+      p.num_n_blocks = static_cast<int>((hidden + p.bn - 1) / p.bn);
+      p.w_scales = static_cast<const uint8_t*>(w2_scale);
+      p.lds = inter / 32;
+      p.w_rows_per_expert = hidden;
+      p.sorted_ids = pr.sorted;
+      p.block_expert = pr.block_expert;
+      p.num_post_padded = pr.post;
+      p.num_routes = static_cast<int>(routes);
+      p.top_k = 1;
+      p.out = ybuf;
+      p.out_dtype = MXFP4_DTYPE_BF16;
+      p.a_scale = nullptr;
+      p.b_scale = nullptr;
+      p.topk_w = topk_weights;
+      p.w_dtype = w_dtype;
+      p.mul_w = 1;
+      p.c_stride_t = hidden;
+      p.c_stride_j = 0;
+      p.vec_ok = 1;
+      if (int rc = routed_pair_gemm<A_TMA, EPI_MOE>(false, ta, tb, p, info.sms, s)) return rc;
+    }
+  } else {
+    const RtRouting rt = carve_rt_routing(ws, routes, num_experts);
+    const int64_t cap = std::max<int64_t>(rt.cap, 1);
+    void* hbuf = ws;
+    ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
+    ybuf = ws;
+    ws += align_up(static_cast<size_t>(routes) * hidden * 2, 256);
+    void* xbuf = ws;
+    if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
+    if (int rc = run_gather(x, hidden, rt.sorted, rt.post, routes, top_k, xbuf, rt.cap, info.sms, s)) return rc;
+    // gate_up with fused SiLU(gate) * up -> h [cap, inter] in routed order
+    {
+      CUtensorMap tw, tx16, tx128;
+      if (int rc = routed_maps(&tw, &tx16, &tx128, w13, static_cast<int64_t>(num_experts) * 2 * inter, hidden, xbuf,
+                               cap, hidden, false, true))
+        return rc;
+      RoutedParams p{};
+      p.pgroup = routed_pgroup(hidden);
+      p.N = static_cast<int>(2 * inter);
+      p.glu_inter = static_cast<int>(inter);
+      p.K = static_cast<int>(hidden);
+      p.num_wblocks = static_cast<int>((inter + 127) / 128);
+      p.w_scales = static_cast<const uint8_t*>(w13_scale);
+      p.lds = hidden / 32;
+      p.w_rows_per_expert = 2 * inter;
+      p.chunks = rt.chunks;
+      p.num_chunks = rt.num_chunks;
+      p.max_chunks = static_cast<int>(rt.max_chunks);
+      p.sorted_ids = rt.sorted;
+      p.num_routes = static_cast<int>(routes);
+      p.top_k = top_k;
+      p.out = hbuf;
+      p.ldo = inter;
+      p.out_dtype = MXFP4_DTYPE_BF16;
+      if (int rc = launch_routed<EPI_GLU, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
+    }
+    // down with route weights, scattered to y[route]
+    {
+      CUtensorMap tw, tx16, tx128;
+      if (int rc = routed_maps(&tw, &tx16, &tx128, w2, static_cast<int64_t>(num_experts) * hidden, inter, hbuf, cap,
+                               inter, false, false))
+        return rc;
+      RoutedParams p{};
+      p.pgroup = routed_pgroup(inter);
+      p.N = static_cast<int>(hidden);
+      p.K = static_cast<int>(inter);
+      p.num_wblocks = static_cast<int>((hidden + 255) / 256);
+      p.w_scales = static_cast<const uint8_t*>(w2_scale);
+      p.lds = inter / 32;
+      p.w_rows_per_expert = hidden;
+      p.chunks = rt.chunks;
+      p.num_chunks = rt.num_chunks;
+      p.max_chunks = static_cast<int>(rt.max_chunks);
+      p.sorted_ids = rt.sorted;
+      p.num_routes = static_cast<int>(routes);
+      p.top_k = 1;
+      p.out = ybuf;
+      p.out_dtype = MXFP4_DTYPE_BF16;
+      p.topk_w = topk_weights;
+      p.w_dtype = w_dtype;
+      p.mul_w = 1;
+      p.c_stride_t = hidden;
+      p.c_stride_j = 0;
+      if (int rc = launch_routed<EPI_MOE, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
+    }
   }
   const int64_t vecs = num_tokens * (hidden / 8);
   const int grid = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, int64_t(info.sms) * 8));

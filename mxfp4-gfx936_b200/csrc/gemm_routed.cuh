@@ -275,6 +275,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tmem_a = tmem_base + 256;
+  constexpr int AS = kRtASlots, XS = kRtXSlots;
   int nch = p.num_chunks[0];
   nch = nch < p.max_chunks ? nch : p.max_chunks;
   const int num_tiles = nch * p.num_wblocks;
@@ -334,10 +335,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
         const int row0 = ch.x + static_cast<int>(rank) * half;
         for (int kt = 0; kt < KT; ++kt, ++it) {
           if ((it & 1) != par) continue;
-          const int s = it % kRtXSlots;
-          const uint32_t ph = (it / kRtXSlots) & 1;
+          const int s = it % XS;
+          const uint32_t ph = (it / XS) & 1;
           if (!mbar_wait(&xempty[s], ph ^ 1, abort_flag)) { ok = false; break; }
-          const uint32_t bar = ready_leader + (it % kRtASlots) * 8;
+          const uint32_t bar = ready_leader + (it % AS) * 8;
           mbar_arrive_expect_tx_cluster(bar, half * 128);
           uint8_t* dst = smem + kRtOffX + s * kRtXBytes;
           if (half == 128) {
@@ -372,8 +373,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
         if (!mbar_wait_cluster(tempty, (tl & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt, ++it) {
-          const int a = it % kRtASlots, sx = it % kRtXSlots;
-          if (!mbar_wait_cluster(&ready[a], (it / kRtASlots) & 1, abort_flag)) { ok = false; break; }
+          const int a = it % AS, sx = it % XS;
+          if (!mbar_wait_cluster(&ready[a], (it / AS) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t bdesc = desc_sw128(smem_u32(smem + kRtOffX + sx * kRtXBytes));
           const uint32_t a_slot = tmem_a + a * 32;
@@ -424,7 +425,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
         const int64_t grow = rt_weight_row<EPI>(p, ch.z, t % p.num_wblocks, rank, r, next_valid);
         next_srow = p.w_scales + (next_valid ? grow * p.lds : 0);
       }
-      return next_valid ? ldg_nc_u32(next_srow + 2 * (kt % KTw)) : 0x7F7F7F7Fu;
+      // rows past the expert's last feature read the first row's scales (their
+      // products land in accumulator rows the epilogue drops); no select on
+      // the loaded word, so nothing waits for it before its pair
+      return ldg_nc_u32(next_srow + 2 * (kt % KTw));
     };
     uint32_t sc_next = scale_word(2 * g);
     for (int it0 = 2 * g; it0 < total; it0 += 8) {
@@ -436,13 +440,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
         const int it = it0 + h;
         if (it >= total) break;
         const int gi = it / p.pgroup;  // packed group of this stage (both stages of a pair share it)
-        const int sp = gi % kRtPSlots, a = it % kRtASlots;
+        const int sp = gi % kRtPSlots, a = it % AS;
         const uint32_t sc = sc_pair >> (16 * h);
         // warp-uniform waits: the tcgen05.st / wait::st below are .sync.aligned
         if (h == 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&pfull[sp], (gi / kRtPSlots) & 1, abort_flag))) { nb = -1; break; }
-        const uint32_t prow = smem_u32(smem + kRtOffP + sp * kRtPBytes) + r * 32 * p.pgroup + (it % p.pgroup) * 32;
-        const uint4 q0 = ld_shared_v4(prow);
-        const uint4 q1 = ld_shared_v4(prow + 16);
+        // rows of 32 * pgroup bytes, swizzled by the TMA (128B for 4 stages, 64B for 2): 16-byte chunk c
+        // of row r sits at chunk c ^ (r % 8) resp. c ^ ((r / 2) % 4), so a warp's 32 rows spread over
+        // all bank groups
+        const uint32_t prow = smem_u32(smem + kRtOffP + sp * kRtPBytes) + r * 32 * p.pgroup;
+        const uint32_t c0 = 2u * static_cast<uint32_t>(it % p.pgroup);
+        const uint32_t sw = p.pgroup == 4 ? static_cast<uint32_t>(r & 7) : static_cast<uint32_t>((r >> 1) & 3);
+        const uint4 q0 = ld_shared_v4(prow + ((c0 ^ sw) << 4));
+        const uint4 q1 = ld_shared_v4(prow + (((c0 + 1) ^ sw) << 4));
         const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         uint32_t v[32];
 #pragma unroll
@@ -462,7 +471,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&pempty[sp]);
         }
-        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&aempty[a], ((it / kRtASlots) & 1) ^ 1, abort_flag))) { nb = -1; break; }
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&aempty[a], ((it / AS) & 1) ^ 1, abort_flag))) { nb = -1; break; }
         tc_fence_after();
         tmem_st_32x32b_x32(tmem_a + lane_base + a * 32, v);
         ++nb;
@@ -472,7 +481,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kRtThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0)
-        for (int h = 0; h < nb; ++h) mbar_arrive_cluster(ready_leader + ((it0 + h) % kRtASlots) * 8);
+        for (int h = 0; h < nb; ++h) mbar_arrive_cluster(ready_leader + ((it0 + h) % AS) * 8);
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 4-7, both CTAs)

@@ -295,14 +295,15 @@ constexpr int kTmPSlots = 4;   // packed ring: each slot holds a group of 4 stag
 constexpr int kTmPGroup = 4;
 constexpr int kTmPGroupBytes = kSmPBytes * kTmPGroup;  // 128 rows x 4 stages x 32 B
 constexpr int kTmXSlots = 4;
-constexpr int kTmASlots = 8;
+constexpr int kTmASlots = 16;  // at most; a launch uses every tensor-memory column past the accumulator
 constexpr int kTmDecodeWarps = 16;  // 4 warps per TMEM lane quarter, taking consecutive pairs of stages
 
 __host__ __device__ constexpr int tm_small_acc_cols(int mp) {
   return mp <= 32 ? 32 : (mp <= 64 ? 64 : (mp <= 128 ? 128 : 256));
 }
-__host__ __device__ constexpr uint32_t tm_small_alloc_cols(int mp) {
-  return tm_small_acc_cols(mp) + kTmASlots * 32 <= 256 ? 256u : 512u;
+__host__ __device__ constexpr uint32_t tm_small_alloc_cols(int) { return 512u; }
+__host__ __device__ constexpr int tm_small_a_slots(int mp) {
+  return (512 - tm_small_acc_cols(mp)) / 32 < kTmASlots ? (512 - tm_small_acc_cols(mp)) / 32 : kTmASlots;
 }
 
 template <bool FP16>
@@ -339,6 +340,7 @@ __global__ void __launch_bounds__(256 + 32 * kTmDecodeWarps, 1)
   const int nst = kt1 - kt0;
   const int acc_cols = tm_small_acc_cols(p.mp);
   const uint32_t alloc_cols = tm_small_alloc_cols(p.mp);
+  const int AS = tm_small_a_slots(p.mp);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTmPSlots; ++s) {
@@ -421,8 +423,8 @@ __global__ void __launch_bounds__(256 + 32 * kTmDecodeWarps, 1)
       const uint32_t idesc = idesc_f16(FP16 ? 0 : 1, kSmRows, p.mp);
       bool ok = true, issued = false;
       for (int it = 0; it < nst; ++it) {
-        const int sa = it % kTmASlots, sx = it % kTmXSlots;
-        if (!mbar_wait(&aready[sa], (it / kTmASlots) & 1, abort_flag)) { ok = false; break; }
+        const int sa = it % AS, sx = it % kTmXSlots;
+        if (!mbar_wait(&aready[sa], (it / AS) & 1, abort_flag)) { ok = false; break; }
         if (!mbar_wait(&xfull[sx], (it / kTmXSlots) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint64_t bdesc = desc_sw128(smem_u32(smem + x_off + sx * x_bytes));  // x: MMA B (N = mp)
@@ -452,35 +454,47 @@ __global__ void __launch_bounds__(256 + 32 * kTmDecodeWarps, 1)
     const int r = q * 32 + lane;  // weight row of the tile = TMEM lane
     const int grow = n0 + r;
     const bool valid = grow < p.N;
+    // rows past N read row 0's scales (their products land in dropped accumulator rows)
     const uint8_t* srow = p.w_scales + (valid ? static_cast<int64_t>(grow) * p.lds : 0);
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    // a pair's four scale codes are one aligned 32-bit word when the pair
-    // starts at an even global stage; its load overlaps the previous pair
-    auto scale_word = [&](int it) -> uint32_t {
-      if (!valid || it >= nst) return 0x7F7F7F7Fu;
-      const int kt = kt0 + it;
-      if ((kt & 1) == 0) return ldg_nc_u32(srow + 2 * kt);
-      const uint32_t lo = *reinterpret_cast<const uint16_t*>(srow + 2 * kt);
-      const uint32_t hi = it + 1 < nst ? *reinterpret_cast<const uint16_t*>(srow + 2 * kt + 2) : 0x7F7Fu;
-      return lo | (hi << 16);
+    // A pair's four scale codes are bytes 2kt .. 2kt+3 of the row: one aligned
+    // word when kt is even, else the top half of the word at 2kt-2 and the
+    // bottom half of the word at 2kt+2 (the word at 2kt-2 again when the pair
+    // has no second stage).  The raw words are loaded one pair ahead and only
+    // combined when the pair is decoded, so no instruction waits on the loads
+    // before then.  Stages past the CTA's last re-read its last stage's words.
+    auto scale_words = [&](int it) -> uint2 {
+      const int kt = kt0 + (it < nst ? it : nst - 1);
+      if ((kt & 1) == 0) {
+        const uint32_t w = ldg_nc_u32(srow + 2 * kt);
+        return make_uint2(w, w);
+      }
+      const uint8_t* hi = it + 1 < nst ? srow + 2 * kt + 2 : srow + 2 * kt - 2;
+      return make_uint2(ldg_nc_u32(srow + 2 * kt - 2), ldg_nc_u32(hi));
     };
-    uint32_t sc_next = scale_word(2 * g);
+    auto pair_codes = [&](int it, uint2 w) -> uint32_t {
+      return ((kt0 + it) & 1) == 0 ? w.x : __funnelshift_r(w.x, w.y, 16);
+    };
+    uint2 sc_next = scale_words(2 * g);
     for (int it0 = 2 * g; it0 < nst; it0 += 8) {
-      const uint32_t sc_pair = sc_next;
-      sc_next = scale_word(it0 + 8);
+      const uint32_t sc_pair = pair_codes(it0, sc_next);
+      sc_next = scale_words(it0 + 8);
       int nb = 0;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int it = it0 + h;
         if (it >= nst) break;
         const int gi = it / kTmPGroup;  // packed group (both stages of a pair share it)
-        const int sp = gi % kTmPSlots, sa = it % kTmASlots;
+        const int sp = gi % kTmPSlots, sa = it % AS;
         const uint32_t sc = sc_pair >> (16 * h);
         // warp-uniform waits: the tcgen05.st / wait::st below are .sync.aligned
         if (h == 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(&pfull[sp], (gi / kTmPSlots) & 1, abort_flag))) { nb = -1; break; }
-        const uint32_t prow = smem_u32(smem + p_off + sp * kTmPGroupBytes) + r * 32 * kTmPGroup + (it % kTmPGroup) * 32;
-        const uint4 q0 = ld_shared_v4(prow);
-        const uint4 q1 = ld_shared_v4(prow + 16);
+        // 128-byte rows, 128B-swizzled by the TMA: 16-byte chunk c of row r sits at chunk c ^ (r % 8),
+        // so the 32 rows of a warp read from eight different bank groups
+        const uint32_t prow = smem_u32(smem + p_off + sp * kTmPGroupBytes) + r * 32 * kTmPGroup;
+        const uint32_t c0 = 2u * static_cast<uint32_t>(it % kTmPGroup), sw = static_cast<uint32_t>(r & 7);
+        const uint4 q0 = ld_shared_v4(prow + ((c0 ^ sw) << 4));
+        const uint4 q1 = ld_shared_v4(prow + (((c0 + 1) ^ sw) << 4));
         const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         uint32_t v[32];
 #pragma unroll
@@ -500,7 +514,7 @@ __global__ void __launch_bounds__(256 + 32 * kTmDecodeWarps, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&pempty[sp]);
         }
-        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&aempty[sa], ((it / kTmASlots) & 1) ^ 1, abort_flag))) { nb = -1; break; }
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&aempty[sa], ((it / AS) & 1) ^ 1, abort_flag))) { nb = -1; break; }
         tc_fence_after();
         tmem_st_32x32b_x32(tmem_a + lane_base + sa * 32, v);
         ++nb;
@@ -510,7 +524,7 @@ __global__ void __launch_bounds__(256 + 32 * kTmDecodeWarps, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0)
-        for (int h = 0; h < nb; ++h) mbar_arrive(&aready[(it0 + h) % kTmASlots]);
+        for (int h = 0; h < nb; ++h) mbar_arrive(&aready[(it0 + h) % AS]);
     }
   }
 
