@@ -13,6 +13,7 @@
 #include "gemm_routed.cuh"
 #include "gemm_small.cuh"
 #include "gemm_w4a4.cuh"
+#include "gemv_routed.cuh"
 
 using namespace mx;
 
@@ -384,6 +385,21 @@ int launch_routed(const CUtensorMap& tw, const CUtensorMap& tx16, const CUtensor
   const int64_t tiles = static_cast<int64_t>(p.max_chunks) * p.num_wblocks;
   const int clusters = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms / 2)));
   kern<<<2 * clusters, kRtThreads, kRtSmemBytes, stream>>>(tw, tx16, tx128, p);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+// Routed GEMV over (route, block of kMoeGemvWarps outputs).
+template <int EPI, bool FP16>
+int launch_moe_gemv(const MoeGemvParams& p, cudaStream_t stream) {
+  MX_CHECK(aligned(p.x, 16) && (p.ldx * 2) % 16 == 0 && aligned(p.w, 16) && p.ldw % 16 == 0,
+           "routed GEMV operands must be 16-byte aligned");
+  if (p.num_routes == 0) return MXFP4_OK;
+  auto kern = mxfp4_moe_gemv_kernel<EPI, FP16>;
+  const int smem = p.K * 2;
+  if (smem > 48 * 1024) MX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const dim3 grid(p.num_routes, (p.rows + kMoeGemvWarps - 1) / kMoeGemvWarps, 1);
+  kern<<<grid, 32 * kMoeGemvWarps, smem, stream>>>(p);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
 }
@@ -997,6 +1013,12 @@ constexpr int64_t kPairRoutesPerExpert = 128;
 bool moe_pair_path(int64_t routes, int num_experts) {
   return routes >= kPairRoutesPerExpert * static_cast<int64_t>(num_experts);
 }
+// Up to kMoeGemvMaxRoutes routes (decode batches) the routed GEMV
+// (gemv_routed.cuh) runs instead: no routing pass, no routed copy, each
+// expert's weights read straight from HBM by the routes that use them.  The
+// op's FP32-precision mode with F16/F32 activations (split BF16 parts) keeps
+// the grouped GEMMs.
+bool moe_gemv_path(int64_t routes, const MoeCompute& mc) { return routes <= kMoeGemvMaxRoutes && mc.parts == 1; }
 
 // Routing of the pair path: 256-route blocks, no chunk table.
 struct PairRouting {
@@ -1066,6 +1088,7 @@ size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_exp
   const int64_t cap = route_capacity(routes, num_experts, pair ? kP2BM : kRtBlock);
   const MoeCompute mc = moe_compute(a_dtype, c_dtype);
   const int64_t ka = k * mc.parts;  // columns of the converted activations
+  if (moe_gemv_path(routes, mc)) return a_dtype != mc.dtype ? align_up(static_cast<size_t>(num_tokens) * k * 2, 256) : 0;
   size_t b = pair ? pair_routing_bytes(routes, num_experts) : rt_routing_bytes(routes, num_experts);
   if (a_dtype != mc.dtype || mc.parts > 1) b += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
   b += align_up(static_cast<size_t>(std::max<int64_t>(cap, 1)) * ka * 2, 256);  // activations in routed order
@@ -1109,6 +1132,35 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   MX_CUDA(cudaMemsetAsync(C, 0, static_cast<size_t>(routes) * n * esz, s));
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (moe_gemv_path(routes, mc)) {
+    const void* a_eff;
+    if (int rc = convert_activations(A, a_dtype, a_mx_scale, mc, num_tokens, k, ws, info, s, stream, a_eff)) return rc;
+    MoeGemvParams g{};
+    g.K = static_cast<int>(k);
+    g.rows = static_cast<int>(n);
+    g.num_experts = num_experts;
+    g.top_k = top_k;
+    g.num_routes = static_cast<int>(routes);
+    g.x = a_eff;
+    g.ldx = k;
+    g.w = static_cast<const uint8_t*>(B);
+    g.w_rows_per_expert = n;
+    g.ldw = k / 2;
+    g.w_scales = static_cast<const uint8_t*>(B_mx_scale);
+    g.lds = k / 32;
+    g.ids = topk_ids;
+    g.ids_dtype = ids_dtype;
+    g.out = C;
+    g.ldo = n;
+    g.out_dtype = c_dtype;
+    g.a_scale = a_scale;
+    g.b_scale = b_scale;
+    g.topk_w = topk_weights;
+    g.w_dtype = w_dtype;
+    g.mul_w = mul_routed_weight ? 1 : 0;
+    if (cdt == MXFP4_DTYPE_F16) return launch_moe_gemv<EPI_MOE, true>(g, s);
+    return launch_moe_gemv<EPI_MOE, false>(g, s);
+  }
   if (moe_pair_path(routes, num_experts)) {
     // many routes per expert: the pair kernel over 256-route blocks
     const PairRouting pr = carve_pair_routing(ws, routes, num_experts);
@@ -1331,6 +1383,8 @@ int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const vo
 size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t hidden,
                                       int64_t inter) {
   const int64_t routes = num_tokens * top_k;
+  if (routes <= kMoeGemvMaxRoutes)  // routed GEMV: h and the weighted down rows, by route
+    return align_up(static_cast<size_t>(routes) * inter * 2, 256) + align_up(static_cast<size_t>(routes) * hidden * 2, 256);
   const bool pair = moe_pair_path(routes, num_experts);
   const int64_t cap = std::max<int64_t>(route_capacity(routes, num_experts, pair ? kP2BM : kRtBlock), 1);
   size_t b = pair ? pair_routing_bytes(routes, num_experts) : rt_routing_bytes(routes, num_experts);
@@ -1363,7 +1417,54 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   if (num_tokens == 0) return MXFP4_OK;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   void* ybuf = nullptr;  // [routes, hidden]: the weighted down rows, by route id
-  if (moe_pair_path(routes, num_experts)) {
+  if (routes <= kMoeGemvMaxRoutes) {
+    // few routes: routed GEMVs straight from the token rows, h by route
+    void* hbuf = ws;
+    ws += align_up(static_cast<size_t>(routes) * inter * 2, 256);
+    ybuf = ws;
+    MoeGemvParams g{};
+    g.K = static_cast<int>(hidden);
+    g.rows = static_cast<int>(inter);
+    g.num_experts = num_experts;
+    g.top_k = top_k;
+    g.num_routes = static_cast<int>(routes);
+    g.x = x;
+    g.ldx = hidden;
+    g.w = static_cast<const uint8_t*>(w13);
+    g.w_rows_per_expert = 2 * inter;
+    g.ldw = hidden / 2;
+    g.w_scales = static_cast<const uint8_t*>(w13_scale);
+    g.lds = hidden / 32;
+    g.ids = topk_ids;
+    g.ids_dtype = ids_dtype;
+    g.glu_inter = static_cast<int>(inter);
+    g.out = hbuf;
+    g.ldo = inter;
+    g.out_dtype = MXFP4_DTYPE_BF16;
+    if (int rc = launch_moe_gemv<EPI_GLU, false>(g, s)) return rc;
+    MoeGemvParams d{};
+    d.K = static_cast<int>(inter);
+    d.rows = static_cast<int>(hidden);
+    d.num_experts = num_experts;
+    d.top_k = 1;
+    d.num_routes = static_cast<int>(routes);
+    d.x = hbuf;
+    d.ldx = inter;
+    d.w = static_cast<const uint8_t*>(w2);
+    d.w_rows_per_expert = hidden;
+    d.ldw = inter / 2;
+    d.w_scales = static_cast<const uint8_t*>(w2_scale);
+    d.lds = inter / 32;
+    d.ids = topk_ids;
+    d.ids_dtype = ids_dtype;
+    d.out = ybuf;
+    d.ldo = hidden;
+    d.out_dtype = MXFP4_DTYPE_BF16;
+    d.topk_w = topk_weights;
+    d.w_dtype = w_dtype;
+    d.mul_w = 1;
+    if (int rc = launch_moe_gemv<EPI_MOE, false>(d, s)) return rc;
+  } else if (moe_pair_path(routes, num_experts)) {
     // many routes per expert: pair kernel over 256-route blocks
     const PairRouting pr = carve_pair_routing(ws, routes, num_experts);
     const int64_t cap = std::max<int64_t>(pr.cap, 1);
