@@ -376,12 +376,38 @@ def make_moe_inputs(device, seed=0, **cfg):
     return x, w13, s13, w2, s2, tw, tid
 
 
-def bench_moe(soft, steps, warmup, device):
-    sets = [make_moe_inputs(device, seed=i, **MOE) for i in range(2)]
+def bench_moe(soft, steps, warmup, device, tokens=None):
+    cfg = dict(MOE, t=tokens) if tokens else MOE
+    sets = [make_moe_inputs(device, seed=i, **cfg) for i in range(2)]
     gs = graphs_for(lambda *a: soft.moe_layer_mxfp4(*a), sets, torch.cuda.Stream())
     ms = time_graphs(gs, steps, warmup)
     del gs, sets
     return ms
+
+
+def moe_weight_bytes(tid, cfg=MOE):
+    """HBM bytes a layer call must read: the packed weights and scales of every
+    expert its routes touch (w13 and w2), plus x in and the output."""
+    h, inter = cfg["h"], cfg["inter"]
+    per_expert = 2 * inter * (h // 2 + h // 32) + h * (inter // 2 + inter // 32)
+    experts = int(torch.unique(tid).numel())
+    return experts * per_expert + 2 * 2 * tid.shape[0] * h
+
+
+def bench_moe_decode(soft, device, tokens_list=(1, 8, 64, 256), steps=50, warmup=5):
+    """The config-2 layer shape at decode batch sizes (config 4's decode MoE):
+    CUDA-graph replays over two input sets with their own weights (426 MB, more
+    than L2), so every call reads its experts' weights from HBM."""
+    hbm = peaks()[0]["hbm_gbs"]
+    out = {}
+    for t in tokens_list:
+        cfg = dict(MOE, t=t)
+        byts = sum(moe_weight_bytes(make_moe_inputs(device, seed=i, **cfg)[6], cfg) for i in range(2)) / 2
+        ms = bench_moe(soft, steps, warmup, device, tokens=t)
+        out[f"t{t}"] = {"us": ms * 1e3, "tokens_per_s": t / (ms * 1e-3), "hbm_bytes": byts,
+                        "gbs": byts / ms / 1e6, "frac_hbm": byts / ms / 1e6 / hbm,
+                        "kernel": "routed GEMV" if t * MOE["k"] <= 64 else "tensor-memory routed GEMM"}
+    return out
 
 
 def bench_e2e_moe(soft, steps, warmup, device):
@@ -672,6 +698,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the non-headline configurations")
     ap.add_argument("--decode-m", type=int, default=1, help="rows of x for --workload decode (qkv weights)")
+    ap.add_argument("--moe-tokens", type=int, default=None, help="tokens for --workload moe (default: config 2's 4096)")
     ap.add_argument("--workload", default=None, choices=["qkv", "oproj", "safe", "decode", "moe", "w4a4"],
                     help="run only this configuration (for profiling); prints its timing as JSON")
     args = ap.parse_args()
@@ -754,6 +781,7 @@ def main():
         rbytes = MOE["t"] * MOE["e"] * 4 + MOE["t"] * MOE["k"] * 8
         extra["config2_router"] = {"ms": ms_r, "us": ms_r * 1e3, "gbs": rbytes / ms_r / 1e6,
                                    "what": "softmax + top-8 + renormalise over 128 expert logits, 4096 tokens"}
+        extra["config4_moe_decode"] = bench_moe_decode(soft, device)
         extra["config4_stack"] = bench_stack(device, 3, 1)
         ms_w = bench_w4a4(soft, 50, 5, device)
         fw = 2.0 * W4A4[0] * W4A4[1] * W4A4[2]
@@ -791,7 +819,7 @@ def run_one(args, soft, device):
         ms = bench_linear(soft, (args.decode_m, QKV[1], QKV[2]), args.steps, args.warmup, 32, "fused", device,
                           seed0=101)
     elif w == "moe":
-        ms = bench_moe(soft, args.steps, args.warmup, device)
+        ms = bench_moe(soft, args.steps, args.warmup, device, tokens=args.moe_tokens)
     else:
         ms = bench_w4a4(soft, args.steps, args.warmup, device)
     print(json.dumps({"workload": w, "ms_per_step": ms, "steps": args.steps}), flush=True)

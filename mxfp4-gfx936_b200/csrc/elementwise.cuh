@@ -335,17 +335,31 @@ __global__ void __launch_bounds__(256) combine_topk_kernel(const __nv_bfloat16* 
     float acc[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
-    for (int j = 0; j < top_k; ++j) {
-      // a route to an expert outside [0, E) was not computed and contributes
-      // zero, as its all-zero rows do in the reference composition
-      const int e = load_expert(ids, ids_dtype, t * top_k + j);
-      if (e < 0 || e >= num_experts) continue;
-      const uint4 q = *reinterpret_cast<const uint4*>(rows + ((t * top_k + j) * hidden) + v * 8);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    // slots in groups of eight: the group's ids, then its rows, are loaded
+    // together (two memory round trips per group), then summed in slot order
+    for (int j0 = 0; j0 < top_k; j0 += 8) {
+      bool ok[8];
+      uint4 q[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        acc[2 * c] += __uint_as_float(w[c] << 16);
-        acc[2 * c + 1] += __uint_as_float(w[c] & 0xFFFF0000u);
+      for (int u = 0; u < 8; ++u) {
+        // a route to an expert outside [0, E) was not computed and contributes
+        // zero, as its all-zero rows do in the reference composition
+        const int e = j0 + u < top_k ? load_expert(ids, ids_dtype, t * top_k + j0 + u) : -1;
+        ok[u] = e >= 0 && e < num_experts;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        q[u] = ok[u] ? *reinterpret_cast<const uint4*>(rows + ((t * top_k + j0 + u) * hidden) + v * 8)
+                     : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (!ok[u]) continue;
+        const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          acc[2 * c] += __uint_as_float(w[c] << 16);
+          acc[2 * c + 1] += __uint_as_float(w[c] & 0xFFFF0000u);
+        }
       }
     }
     uint4 o;
