@@ -1630,8 +1630,85 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
 namespace {
 // Route chunks of an owner's received rows (all E experts bound the local ones).
 int64_t ep_max_chunks(int64_t recv_capacity, int num_experts) {
-  return recv_capacity / (kEpBlock * kEpChunkBlocks) + num_experts + 1;
+  return recv_capacity / kEpChunkRows + num_experts + 1;
 }
+// Padding block of the owners' received rows, the same on every rank: the
+// capacity from mxfp4_ep_moe_recv_capacity is at least 383 rows per local
+// expert exactly when it was sized for 256-row blocks (>= 128 routes per
+// local expert on average, the CTA-pair GEMM), and below that for 32-row
+// blocks (the routed tensor-memory GEMM).
+int ep_block_rows(int64_t recv_capacity, int el) {
+  return recv_capacity >= static_cast<int64_t>(kPairRoutesPerExpert + kEpPairBlock - 1) * el ? kEpPairBlock : kEpBlock;
+}
+
+// The owner's two GEMMs on the CTA-pair kernel over 256-row blocks of the
+// received rows (routed order, row ids = rows, pads = cap).
+int ep_owner_pair_gemms(const void* xrow, const void* w13, const void* w13_scale, const void* w2, const void* w2_scale,
+                        void* hbuf, void* yrow, const void* wrow, const int32_t* rid, const int32_t* block_expert,
+                        const int32_t* post, int64_t cap, int cap_blocks, int el, int64_t hidden, int64_t inter, int sms,
+                        cudaStream_t s) {
+  {
+    CUtensorMap ta, tb;
+    if (int rc = make_map_2d(&ta, xrow, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hidden, cap, hidden * 2, kP2BK,
+                             kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = make_map_2d(&tb, w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hidden / 2,
+                             static_cast<uint64_t>(el) * 2 * inter, hidden / 2, kP2BK / 2, kP2HalfRows,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    PairParams p{};
+    p.N = static_cast<int>(2 * inter);
+    p.K = static_cast<int>(hidden);
+    p.bn = 256;
+    p.num_m_blocks = cap_blocks;
+    p.num_n_blocks = static_cast<int>((inter + p.bn / 2 - 1) / (p.bn / 2));
+    p.w_scales = static_cast<const uint8_t*>(w13_scale);
+    p.lds = hidden / 32;
+    p.w_rows_per_expert = 2 * inter;
+    p.glu_inter = static_cast<int>(inter);
+    p.sorted_ids = rid;
+    p.block_expert = block_expert;
+    p.num_post_padded = post;
+    p.num_routes = static_cast<int>(cap);
+    p.top_k = 1;
+    p.out = hbuf;
+    p.ldo = inter;
+    p.out_dtype = MXFP4_DTYPE_BF16;
+    p.vec_ok = 1;
+    if (int rc = routed_pair_gemm<A_TMA, EPI_GLU>(false, ta, tb, p, sms, s)) return rc;
+  }
+  CUtensorMap ta, tb;
+  if (int rc = make_map_2d(&ta, hbuf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inter, cap, inter * 2, kP2BK, kP2HalfRows,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int rc = make_map_2d(&tb, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inter / 2, static_cast<uint64_t>(el) * hidden,
+                           inter / 2, kP2BK / 2, kP2HalfRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  PairParams p{};
+  p.N = static_cast<int>(hidden);
+  p.K = static_cast<int>(inter);
+  p.bn = 256;
+  p.num_m_blocks = cap_blocks;
+  p.num_n_blocks = static_cast<int>((hidden + p.bn - 1) / p.bn);
+  p.w_scales = static_cast<const uint8_t*>(w2_scale);
+  p.lds = inter / 32;
+  p.w_rows_per_expert = hidden;
+  p.sorted_ids = rid;
+  p.block_expert = block_expert;
+  p.num_post_padded = post;
+  p.num_routes = static_cast<int>(cap);
+  p.top_k = 1;
+  p.out = yrow;
+  p.out_dtype = MXFP4_DTYPE_BF16;
+  p.topk_w = wrow;
+  p.w_dtype = MXFP4_DTYPE_F32;
+  p.mul_w = 1;
+  p.c_stride_t = hidden;
+  p.c_stride_j = 0;
+  p.vec_ok = 1;
+  return routed_pair_gemm<A_TMA, EPI_MOE>(false, ta, tb, p, sms, s);
+}
+
 }  // namespace
 
 extern "C" {
@@ -1639,8 +1716,10 @@ extern "C" {
 int64_t mxfp4_ep_moe_recv_capacity(int64_t max_tokens_per_rank, int top_k, int num_experts, int world) {
   if (max_tokens_per_rank < 0 || top_k <= 0 || num_experts <= 0 || world <= 0 || num_experts % world) return 0;
   const int64_t el = num_experts / world;
-  const int64_t rows = static_cast<int64_t>(world) * max_tokens_per_rank * top_k + el * (kEpBlock - 1);
-  return (rows + kEpBlock - 1) / kEpBlock * kEpBlock;
+  const int64_t routes = static_cast<int64_t>(world) * max_tokens_per_rank * top_k;
+  const int blk = routes >= kPairRoutesPerExpert * el ? kEpPairBlock : kEpBlock;
+  const int64_t rows = routes + el * (blk - 1);
+  return (rows + blk - 1) / blk * blk;
 }
 
 size_t mxfp4_ep_moe_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t inter,
@@ -1679,10 +1758,11 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
            "topk_weights must be F32, BF16 or F16");
   MX_CHECK(ids_dtype == MXFP4_DTYPE_I32 || ids_dtype == MXFP4_DTYPE_I64, "topk_ids must be I32 or I64");
   MX_CHECK(aligned(x, 16) && aligned(out, 16), "x and out must be 16-byte aligned");
-  MX_CHECK(recv_capacity > 0 && recv_capacity % kEpBlock == 0 && recv_capacity < (int64_t(1) << 24),
-           "recv_capacity must be a positive multiple of 32 below 2^24");
+  const int blk = ep_block_rows(recv_capacity, num_experts / world);
+  MX_CHECK(recv_capacity > 0 && recv_capacity % blk == 0 && recv_capacity < (int64_t(1) << 24),
+           "recv_capacity must be a positive multiple of 32 (of 256 from 383 rows per local expert) below 2^24");
   const int64_t routes = num_tokens * top_k;
-  MX_CHECK(static_cast<int64_t>(world) * routes + (num_experts / world) * (kEpBlock - 1) <= recv_capacity ||
+  MX_CHECK(static_cast<int64_t>(world) * routes + (num_experts / world) * (blk - 1) <= recv_capacity ||
                routes == 0,
            "recv_capacity too small for this many routes");
   const size_t need = mxfp4_ep_moe_workspace_size(num_tokens, top_k, num_experts, inter, recv_capacity);
@@ -1702,7 +1782,7 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
   cudaStream_t s = as_stream(stream);
   const int el = num_experts / world;
   const int64_t cap = recv_capacity;
-  const int cap_blocks = static_cast<int>(cap / kEpBlock);
+  const int cap_blocks = static_cast<int>(cap / blk);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   auto take = [&](size_t bytes) {
     uint8_t* q = ws;
@@ -1731,7 +1811,8 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
   MX_CUDA(cudaGetLastError());
   // 2. plan + stable local order; dispatch rows into the owners' xr; barrier
   ep_plan_kernel<<<1, 1024, 0, s>>>(static_cast<const int32_t*>(counts[rank]), num_experts, world, rank, send_base,
-                                    lstart, block_expert, post, rid, static_cast<int>(cap), cap_blocks, chunks, nchunks);
+                                    lstart, block_expert, post, rid, static_cast<int>(cap), cap_blocks, chunks, nchunks,
+                                    blk);
   MX_CUDA(cudaGetLastError());
   if (routes > 0) {
     if (int rc = run_route(topk_ids, ids_dtype, routes, num_experts, 0, 1, sorted, bexp, nvalid, routes, route_ws, s))
@@ -1745,6 +1826,11 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
   peer_barrier_kernel<<<1, 32, 0, s>>>(pf, rank, world, counter);
   MX_CUDA(cudaGetLastError());
   // 3. owner: gate_up (fused SiLU * up) and down (route weight) over the received rows
+  if (blk == kEpPairBlock) {
+    if (int rc = ep_owner_pair_gemms(xr[rank], w13, w13_scale, w2, w2_scale, hbuf, yr[rank], wr[rank], rid,
+                                     block_expert, post, cap, cap_blocks, el, hidden, inter, info.sms, s))
+      return rc;
+  } else {
   {
     CUtensorMap tw, tx16, tx128;
     if (int rc = routed_maps(&tw, &tx16, &tx128, w13, static_cast<int64_t>(el) * 2 * inter, hidden, xr[rank], cap,
@@ -1797,6 +1883,7 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
     p.c_stride_t = hidden;
     p.c_stride_j = 0;
     if (int rc = launch_routed<EPI_MOE, false>(tw, tx16, tx128, p, info.sms, s)) return rc;
+  }
   }
   peer_barrier_kernel<<<1, 32, 0, s>>>(pf, rank, world, counter);
   MX_CUDA(cudaGetLastError());

@@ -24,8 +24,9 @@
 namespace mx {
 
 constexpr int kEpMaxRanks = 8;
-constexpr int kEpBlock = 32;   // padding granularity of every local expert's rows (the routed GEMMs' block)
-constexpr int kEpChunkBlocks = 8;  // a route chunk: at most 8 blocks (256 rows, the routed GEMMs' N)
+constexpr int kEpBlock = 32;       // padding of every local expert's rows for the routed tensor-memory GEMM
+constexpr int kEpPairBlock = 256;  // ... for the CTA-pair GEMM (its M): many routes per expert
+constexpr int kEpChunkRows = 256;  // a route chunk of the routed GEMM: at most 256 rows (its N)
 
 struct EpPeers {
   void* p[kEpMaxRanks];
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t* __restrict
                                                        int32_t* __restrict__ lstart, int32_t* __restrict__ block_expert,
                                                        int32_t* __restrict__ num_post_padded, int32_t* __restrict__ rid,
                                                        int cap, int cap_blocks, int4* __restrict__ chunks,
-                                                       int32_t* __restrict__ num_chunks) {
+                                                       int32_t* __restrict__ num_chunks, int blk) {
   __shared__ int warp_tmp[33];
   __shared__ int scan_nb[kMaxExperts];
   __shared__ int nb_s[kMaxExperts];
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t* __restrict
       if (s == rank) own = c;
     }
   }
-  const int nb = (total + kEpBlock - 1) / kEpBlock;
+  const int nb = (total + blk - 1) / blk;
   int t_nb, t_own;
   const int sc = block_excl_scan_1024(nb, warp_tmp, t_nb);
   const int ls = block_excl_scan_1024(own, warp_tmp, t_own);
@@ -127,36 +128,37 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t* __restrict
   if (e < num_experts) {
     const int first = (e / el) * el;  // the owner's first expert
     const int bstart = sc - scan_nb[first];
-    send_base[e] = bstart * kEpBlock + below;
+    send_base[e] = bstart * blk + below;
     lstart[e] = ls;
   }
   // owner side: this rank's experts [rank*el, rank*el + el)
   const int e0 = rank * el;
   const int used = (e0 + el - 1 < num_experts) ? scan_nb[e0 + el - 1] + nb_s[e0 + el - 1] - scan_nb[e0] : 0;
-  if (threadIdx.x == 0) num_post_padded[0] = used * kEpBlock;
+  if (threadIdx.x == 0) num_post_padded[0] = used * blk;
   for (int b = used + threadIdx.x; b < cap_blocks; b += blockDim.x) block_expert[b] = -1;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int x = wid; x < el; x += 32) {
     const int g = e0 + x;
     const int bstart = scan_nb[g] - scan_nb[e0];
     for (int b = lane; b < nb_s[g]; b += 32) block_expert[bstart + b] = x;
-    const int base = bstart * kEpBlock;
-    for (int i = lane; i < nb_s[g] * kEpBlock; i += 32) rid[base + i] = i < tot_s[g] ? base + i : cap;
+    const int base = bstart * blk;
+    for (int i = lane; i < nb_s[g] * blk; i += 32) rid[base + i] = i < tot_s[g] ? base + i : cap;
   }
   // route chunks of the owner's experts for the routed GEMMs: {first row,
-  // rows, local expert, 0}, at most kEpChunkBlocks blocks each
+  // rows, local expert, 0}, at most kEpChunkRows rows each
   __syncthreads();
   const bool mine = e >= e0 && e < e0 + el;
-  const int nc = mine ? (nb + kEpChunkBlocks - 1) / kEpChunkBlocks : 0;
+  const int chunk_blocks = kEpChunkRows / blk;
+  const int nc = mine ? (nb + chunk_blocks - 1) / chunk_blocks : 0;
   int t_nc;
   const int cb = block_excl_scan_1024(nc, warp_tmp, t_nc);
   if (threadIdx.x == 0) num_chunks[0] = t_nc;
   if (mine) {
     const int bstart = scan_nb[e] - scan_nb[e0];
     for (int i = 0; i < nc; ++i) {
-      const int b0 = i * kEpChunkBlocks;
-      const int nbl = min(kEpChunkBlocks, nb - b0);
-      chunks[cb + i] = make_int4((bstart + b0) * kEpBlock, nbl * kEpBlock, e - e0, 0);
+      const int b0 = i * chunk_blocks;
+      const int nbl = min(chunk_blocks, nb - b0);
+      chunks[cb + i] = make_int4((bstart + b0) * blk, nbl * blk, e - e0, 0);
     }
   }
 }

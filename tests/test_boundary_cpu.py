@@ -186,13 +186,19 @@ def test_routing_and_ep_capacities_hold_every_layout():
         assert cap % block == 0
         for dist_ in (rng.multinomial(routes, np.ones(experts) / experts), np.eye(experts, dtype=int)[0] * routes):
             assert _padded_rows(dist_, block) <= cap
-    for t, k, e, world in [(512, 8, 128, 8), (2048, 8, 128, 2), (1, 1, 4, 4), (300, 4, 32, 1)]:
+    for t, k, e, world in [(512, 8, 128, 8), (2048, 8, 128, 2), (1, 1, 4, 4), (300, 4, 32, 1), (8, 8, 128, 8)]:
         cap = lib.mxfp4_ep_moe_recv_capacity(t, k, e, world)
-        assert cap % 32 == 0  # the owner pads every local expert to 32 rows
         el = e // world
+        # the owner pads every local expert to 256 rows (CTA-pair GEMM) when the
+        # ranks' routes average 128 or more per local expert, else to 32 rows;
+        # the layer reads the block back from the capacity (>= 383 rows per
+        # local expert <=> 256-row blocks)
+        block = 256 if world * t * k >= 128 * el else 32
+        assert cap % block == 0
+        assert (cap >= 383 * el) == (block == 256)
         # worst case for one owner: every route of every rank lands on its experts
         for dist_ in (rng.multinomial(world * t * k, np.ones(el) / el), np.eye(el, dtype=int)[0] * world * t * k):
-            assert _padded_rows(dist_, 32) <= cap
+            assert _padded_rows(dist_, block) <= cap
     assert lib.mxfp4_ep_moe_recv_capacity(10, 2, 10, 4) == 0  # experts must divide over the ranks
     assert lib.mxfp4_ep_moe_recv_capacity(-1, 2, 8, 4) == 0
 

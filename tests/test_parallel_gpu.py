@@ -87,6 +87,18 @@ def _worker(rank, world, port, q):
         n2 = t_local if rank == 0 else t_local - 100
         y_ep2 = layer(x_all[sl][:n2].contiguous(), tw2[sl][:n2].contiguous(), tid2[sl][:n2].contiguous())
         ep_ok = ep_ok and bool(torch.equal(y_ep2.view(torch.int16), y_full2[:n2].view(torch.int16)))
+        # both owner GEMMs: 32-row blocks (routed tensor-memory GEMM) while the
+        # ranks' routes average fewer than 128 per local expert, 256-row blocks
+        # (CTA-pair GEMM) from there on; world = 1 above is the former, so run
+        # the latter here as well
+        if world == 1:
+            t3 = 1152
+            x3 = torch.randn(t3, h, generator=g, device=dev).to(torch.bfloat16)
+            tw3, tid3 = torch.topk(torch.softmax(torch.randn(t3, e, generator=g, device=dev), -1), top_k, -1)
+            y_full3 = soft.moe_layer_mxfp4(x3, w13, s13, w2, s2, tw3, tid3)
+            layer3 = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, max_tokens=t3)
+            y_ep3 = layer3(x3, tw3.contiguous(), tid3.contiguous())
+            ep_ok = ep_ok and bool(torch.equal(y_ep3.view(torch.int16), y_full3.view(torch.int16)))
         torch.cuda.synchronize()
         q.put((rank, lin_ok, ep_ok, soft.device_status()))
     finally:
