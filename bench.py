@@ -495,6 +495,39 @@ STACK_DECODE_BATCHES = (1, 8, 64, 256)
 STACK_DECODE_CTX = 2048          # decode continues 2048-token sequences
 
 
+def bench_stack_decode(device, steps, warmup, batch, layers):
+    """One config-4 decode step (batch tokens, 2048-token context) of a
+    ``layers``-layer stack as a replayed CUDA graph (profiling aid)."""
+    dsm = _load("mxfp4_decoder_stack", PKG / "decoder_stack.py")
+    cfg = dsm.StackConfig(layers=layers)
+    full = [dsm.random_layer(cfg, device, seed=1000 + i) for i in range(cfg.layers)]
+    stack = dsm.DecoderStack(cfg, full, max_ctx=STACK_DECODE_CTX + 8, max_tokens=max(batch, 1))
+    del full
+    stack.allocate_cache(batch, STACK_DECODE_CTX + 1)
+    hb = torch.randn(batch, cfg.hidden, generator=torch.Generator(device=device).manual_seed(5),
+                     device=device).to(torch.bfloat16)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            stack.decode(hb, STACK_DECODE_CTX)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        stack.decode(hb, STACK_DECODE_CTX)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(steps):
+        graph.replay()
+    en.record()
+    en.synchronize()
+    return st.elapsed_time(en) / steps
+
+
 def bench_stack(device, steps, warmup, rank=0, world=1, group=None, barrier=None, layers=48):
     """the Qwen3-30B-A3B-shaped 48-layer stack (random-init
     MXFP4 weights for every linear).  Prefill of 8 x 2048 tokens (eager, CUDA
@@ -699,7 +732,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the non-headline configurations")
     ap.add_argument("--decode-m", type=int, default=1, help="rows of x for --workload decode (qkv weights)")
     ap.add_argument("--moe-tokens", type=int, default=None, help="tokens for --workload moe (default: config 2's 4096)")
-    ap.add_argument("--workload", default=None, choices=["qkv", "oproj", "safe", "decode", "moe", "w4a4"],
+    ap.add_argument("--stack-layers", type=int, default=48, help="layers for --workload stack-decode")
+    ap.add_argument("--workload", default=None, choices=["qkv", "oproj", "safe", "decode", "moe", "w4a4", "stack-decode"],
                     help="run only this configuration (for profiling); prints its timing as JSON")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -820,6 +854,8 @@ def run_one(args, soft, device):
                           seed0=101)
     elif w == "moe":
         ms = bench_moe(soft, args.steps, args.warmup, device, tokens=args.moe_tokens)
+    elif w == "stack-decode":
+        ms = bench_stack_decode(device, args.steps, args.warmup, args.decode_m, args.stack_layers)
     else:
         ms = bench_w4a4(soft, args.steps, args.warmup, device)
     print(json.dumps({"workload": w, "ms_per_step": ms, "steps": args.steps}), flush=True)
