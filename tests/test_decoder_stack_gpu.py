@@ -156,10 +156,23 @@ def _worker(rank, world, port, q):
         h0, steps = _inputs(dev)
         one = _run(dsm.DecoderStack(CFG, layers, max_ctx=256), h0, steps)
         multi = _run(dsm.DecoderStack(CFG, layers, rank=rank, world=world, max_ctx=256), h0, steps)
-        same = all(torch.equal(a.view(torch.int16), b.view(torch.int16)) for a, b in zip(one, multi))
+        # Every MXFP4 call of the sharded stack is checked bit for bit against
+        # the single-GPU kernels elsewhere (test_parallel_gpu); here the whole
+        # stack is compared within tolerance: attention runs through torch
+        # SDPA on each rank's sequences only (its backend and rounding may
+        # depend on the batch), and at decode sizes the single-GPU MoE layer
+        # takes the routed GEMV while the expert-parallel owners run grouped
+        # GEMMs.  Random weights let the residual stream grow, so a few BF16
+        # roundings show up as ~1e-3 relative differences after two layers.
+        same, notes = True, []
+        for i, (a, b) in enumerate(zip(one, multi)):
+            a32, b32 = a.float(), b.float()
+            rel = float(torch.linalg.norm(b32 - a32) / torch.linalg.norm(a32))
+            notes.append(f"output {i}: rel {rel:.3g}")
+            same = same and rel < 1e-2
         torch.cuda.synchronize()
         dist.barrier()
-        q.put((rank, same, None))
+        q.put((rank, same, None if same else "; ".join(notes)))
     except Exception as exc:  # report, then leave with the others
         q.put((rank, False, repr(exc)))
     finally:
@@ -167,7 +180,7 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_stack_is_bit_exact_with_one_gpu():
+def test_two_gpu_stack_matches_one_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
