@@ -694,13 +694,20 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
   p.K = static_cast<int>(k);
   p.num_m_blocks = static_cast<int>((m + kP2BM - 1) / kP2BM);
   // pair tile width: the multiple of 32 (<= 256) that minimises rounds x width,
-  // so the last round of persistent clusters is not mostly idle
+  // so the last round of persistent clusters is not mostly idle.  With peer
+  // stores (the fused all-gather) only widths down to 64 that give every
+  // cluster two or more tiles qualify: the pusher warps then send a cluster's
+  // first tiles over NVLink while its tensor cores compute the next, instead
+  // of every tile finishing in one round and the whole all-gather waiting for
+  // the GEMM.
   {
     const int64_t clusters_max = std::max(1, info.sms / 2);
-    int best_bn = 256;
+    const int min_bn = peers.n > 0 ? 64 : 128;
+    int best_bn = peers.n > 0 ? 64 : 256;
     int64_t best_cost = -1;
-    for (int bn = 256; bn >= 128; bn -= 32) {
+    for (int bn = 256; bn >= min_bn; bn -= 32) {
       const int64_t tiles_bn = p.num_m_blocks * ((n + bn - 1) / bn);
+      if (peers.n > 0 && tiles_bn < 2 * clusters_max) continue;
       const int64_t rounds = (tiles_bn + clusters_max - 1) / clusters_max;
       const int64_t cost = rounds * (bn + 64);  // + fixed per-tile cost of a narrower tile
       if (best_cost < 0 || cost < best_cost) {
@@ -1747,7 +1754,10 @@ int mxfp4_ep_moe_layer(const void* x, const void* w13, const void* w13_scale, co
                        size_t workspace_bytes, void* stream) {
   DevInfo info;
   if (int rc = current_device_info(info)) return rc;
-  MX_CHECK(x && w13 && w13_scale && w2 && w2_scale && topk_weights && topk_ids && out, "null pointer");
+  // a rank with no tokens still takes part (it owns experts and meets the
+  // barriers): its token-side pointers may be null then
+  MX_CHECK(w13 && w13_scale && w2 && w2_scale, "null pointer");
+  MX_CHECK(num_tokens == 0 || (x && topk_weights && topk_ids && out), "null pointer");
   MX_CHECK(counts && xr && wr && yr && flags && counter, "null peer table");
   MX_CHECK(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world, "bad rank/world");
   MX_CHECK(num_experts > 0 && num_experts <= kMaxExperts && num_experts % world == 0,
