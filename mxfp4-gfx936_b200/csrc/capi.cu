@@ -152,7 +152,7 @@ int run_gather(const void* x, int64_t k_elems, const int32_t* sorted_ids, const 
 
 template <int AMODE, int BMODE, int EPI, bool FP16, int DW, bool PEERS = false>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& p, int clusters,
-                cudaStream_t stream) {
+                cudaStream_t stream, bool after_decode = false) {
   using Cfg = Pair2Cfg<BMODE, DW, PEERS>;
   auto kern = mxfp4_gemm_pair_kernel<AMODE, BMODE, EPI, FP16, DW, PEERS>;
   static std::once_flag once;
@@ -161,7 +161,24 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const PairParams& 
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   });
   MX_CUDA(attr_err);
-  kern<<<2 * clusters, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  if (!after_decode) {
+    kern<<<2 * clusters, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  } else {
+    // programmatic dependent launch behind the weight decode: the GEMM's
+    // set-up (barriers, tensor memory, cluster sync) overlaps the decode's
+    // tail; the kernel waits for the decode's output before reading it
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MX_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  }
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
 }
@@ -755,12 +772,13 @@ int linear_impl(const void* x, int x_dtype, int64_t ldx, const void* w_packed, i
     if (int rc = dequant_into_workspace()) return rc;
   if (int rc = make_map_2d(&tb, wd, xt, 2, k, n, ldwd * 2, kP2BK, p.bn / 2, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
+  const bool after_decode = w_packed != nullptr && wd == workspace;  // the decode kernel just ran on this stream
   if (peers.n > 0) {
-    if (fp16) return launch_pair<A_TMA, B_TMA, EPI_DENSE, true, 0, true>(ta, tb, p, clusters, s);
-    return launch_pair<A_TMA, B_TMA, EPI_DENSE, false, 0, true>(ta, tb, p, clusters, s);
+    if (fp16) return launch_pair<A_TMA, B_TMA, EPI_DENSE, true, 0, true>(ta, tb, p, clusters, s, after_decode);
+    return launch_pair<A_TMA, B_TMA, EPI_DENSE, false, 0, true>(ta, tb, p, clusters, s, after_decode);
   }
-  if (fp16) return launch_pair<A_TMA, B_TMA, EPI_DENSE, true, 0>(ta, tb, p, clusters, s);
-  return launch_pair<A_TMA, B_TMA, EPI_DENSE, false, 0>(ta, tb, p, clusters, s);
+  if (fp16) return launch_pair<A_TMA, B_TMA, EPI_DENSE, true, 0>(ta, tb, p, clusters, s, after_decode);
+  return launch_pair<A_TMA, B_TMA, EPI_DENSE, false, 0>(ta, tb, p, clusters, s, after_decode);
 }
 
 

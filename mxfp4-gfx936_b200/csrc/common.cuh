@@ -209,6 +209,14 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream is still
+// running; griddep_wait() returns once that kernel has completed and its
+// writes are visible (immediately for an ordinary launch).  The previous
+// kernel lets it start early with griddep_launch_dependents().
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Arrive on `bar` when all earlier tcgen05 async operations of this thread complete.

@@ -20,6 +20,7 @@ template <int OUT>
 __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ packed,
                                                       const uint8_t* __restrict__ scales,
                                                       void* __restrict__ out, int64_t num_blocks) {
+  griddep_launch_dependents();  // the GEMM behind it may set up while this runs
   const int64_t num_words = num_blocks * 4;  // 4 words of 8 codes per 32-value scale block
   const uint32_t* words = reinterpret_cast<const uint32_t*>(packed);
   const int lane = threadIdx.x & 31;

@@ -472,6 +472,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Pair2Cfg<BMODE, DECO
   __syncthreads();
   cluster_sync();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
+  // launched right behind the weight decode (programmatic dependent launch):
+  // the set-up above overlaps its tail, its output is read from here on
+  griddep_wait();
   const uint32_t tmem_base = *tmem_slot;
   int nmb = p.num_m_blocks;
   if (EPI != EPI_DENSE) {

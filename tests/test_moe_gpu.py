@@ -139,7 +139,10 @@ def test_moe_layer_matches_reference_golden():
     assert ok, (err, bound, rel)
 
 
-@pytest.mark.parametrize("t,h,e,k,inter", [(1, 256, 8, 2, 128), (200, 512, 16, 4, 256), (513, 256, 64, 8, 384)])
+# routes per call: 2 (routed GEMV), 800 and 4104 (routed tensor-memory GEMM), 4096 over 16 experts (256 per
+# expert: the CTA-pair GEMM)
+@pytest.mark.parametrize("t,h,e,k,inter", [(1, 256, 8, 2, 128), (200, 512, 16, 4, 256), (513, 256, 64, 8, 384),
+                                           (1024, 256, 16, 4, 128)])
 def test_moe_layer_matches_oracle(t, h, e, k, inter):
     g = torch.Generator().manual_seed(t * 3 + e)
     x = torch.randn(t, h, generator=g).to(torch.bfloat16)
