@@ -13,6 +13,7 @@
 #include "gemm_routed.cuh"
 #include "gemm_small.cuh"
 #include "gemm_w4a4.cuh"
+#include "gemm_mx8.cuh"
 #include "gemv_routed.cuh"
 
 using namespace mx;
@@ -111,6 +112,32 @@ int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, i
   CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MXFP4_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+  return MXFP4_OK;
+}
+
+// Tiled tensor map of any rank (2..5): dims[0] innermost, strides in bytes
+// for dims 1..rank-1 (any order).
+int make_map_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc;
+  if (int rc = get_encoder(enc)) return rc;
+  if (!aligned(base, 16)) return fail(MXFP4_ERR_INVALID_ARGUMENT, "TMA operand must be 16-byte aligned");
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t b[5];
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    if (i > 0) {
+      if (strides[i - 1] % 16 != 0) return fail(MXFP4_ERR_INVALID_ARGUMENT, "TMA stride must be a multiple of 16 bytes");
+      st[i - 1] = strides[i - 1];
+    }
+  }
+  CUresult r = enc(map, dtype, rank, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(MXFP4_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
   return MXFP4_OK;
@@ -312,7 +339,7 @@ int64_t route_capacity(int64_t num_routes, int num_experts, int block_m) {
 int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_experts,
               int expert_offset, int block_m, int32_t* sorted_ids, int32_t* block_expert,
               int32_t* post, int64_t capacity, uint8_t* ws, cudaStream_t stream,
-              int4* rt_chunks = nullptr, int32_t* rt_num_chunks = nullptr) {
+              int4* rt_chunks = nullptr, int32_t* rt_num_chunks = nullptr, int chunk_blocks = kRtChunkBlocks) {
   RouteWs r = carve_route_ws(ws, num_routes, num_experts);
   const int64_t chunks = std::max<int64_t>((num_routes + kRouteThreads - 1) / kRouteThreads, 1);
   const size_t smem = sizeof(int32_t) * kRouteWarps * num_experts;
@@ -331,7 +358,7 @@ int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_expert
   MX_CUDA(cudaGetLastError());
   route_offsets_kernel<<<1, 1024, 0, stream>>>(r.hist, static_cast<int>(chunks), num_experts, block_m,
                                                num_routes, r.blk_off, sorted_ids, block_expert, post,
-                                               capacity / block_m, rt_chunks, rt_num_chunks, kRtChunkBlocks);
+                                               capacity / block_m, rt_chunks, rt_num_chunks, chunk_blocks);
   MX_CUDA(cudaGetLastError());
   if (num_routes > 0)
     route_scatter_kernel<<<static_cast<unsigned>(chunks), kRouteThreads, 0, stream>>>(
@@ -341,10 +368,10 @@ int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_expert
   return MXFP4_OK;
 }
 
-// --- routing of the routed GEMMs (32-route blocks, chunks of <= 256 routes) ---
-int64_t rt_max_chunks(int64_t routes, int num_experts) {
+// --- routing of the routed GEMMs (32-route blocks, chunks of <= chunk_rows routes) ---
+int64_t rt_max_chunks(int64_t routes, int num_experts, int chunk_rows) {
   const int64_t cap = route_capacity(routes, num_experts, kRtBlock);
-  return cap / (kRtBlock * kRtChunkBlocks) + std::min<int64_t>(num_experts, routes) + 1;
+  return cap / chunk_rows + std::min<int64_t>(num_experts, routes) + 1;
 }
 
 struct RtRouting {
@@ -356,18 +383,21 @@ struct RtRouting {
   int4* chunks;        // [max_chunks]
   int32_t* num_chunks;
   uint8_t* route_ws;
+  int chunk_blocks;
 };
 
-size_t rt_routing_bytes(int64_t routes, int num_experts) {
+size_t rt_routing_bytes(int64_t routes, int num_experts, int chunk_rows = kRtBlock * kRtChunkBlocks) {
   const int64_t cap = route_capacity(routes, num_experts, kRtBlock);
   return align_up(sizeof(int32_t) * std::max<int64_t>(cap, 1), 256) + align_up(sizeof(int32_t) * (cap / kRtBlock + 1), 256) +
-         256 + align_up(sizeof(int4) * rt_max_chunks(routes, num_experts), 256) + 256 + route_ws_bytes(routes, num_experts);
+         256 + align_up(sizeof(int4) * rt_max_chunks(routes, num_experts, chunk_rows), 256) + 256 +
+         route_ws_bytes(routes, num_experts);
 }
 
-RtRouting carve_rt_routing(uint8_t*& ws, int64_t routes, int num_experts) {
+RtRouting carve_rt_routing(uint8_t*& ws, int64_t routes, int num_experts, int chunk_rows = kRtBlock * kRtChunkBlocks) {
   RtRouting r;
   r.cap = route_capacity(routes, num_experts, kRtBlock);
-  r.max_chunks = rt_max_chunks(routes, num_experts);
+  r.max_chunks = rt_max_chunks(routes, num_experts, chunk_rows);
+  r.chunk_blocks = chunk_rows / kRtBlock;
   r.sorted = reinterpret_cast<int32_t*>(ws);
   ws += align_up(sizeof(int32_t) * std::max<int64_t>(r.cap, 1), 256);
   r.block_expert = reinterpret_cast<int32_t*>(ws);
@@ -386,7 +416,7 @@ RtRouting carve_rt_routing(uint8_t*& ws, int64_t routes, int num_experts) {
 int run_rt_routing(const void* ids, int ids_dtype, int64_t routes, int num_experts, const RtRouting& r,
                    cudaStream_t s) {
   return run_route(ids, ids_dtype, routes, num_experts, 0, kRtBlock, r.sorted, r.block_expert, r.post, r.cap,
-                   r.route_ws, s, r.chunks, r.num_chunks);
+                   r.route_ws, s, r.chunks, r.num_chunks, r.chunk_blocks);
 }
 
 template <int EPI, bool FP16>
@@ -438,6 +468,124 @@ int routed_maps(CUtensorMap* tw, CUtensorMap* tx16, CUtensorMap* tx128, const vo
   const uint64_t rows = static_cast<uint64_t>(std::max<int64_t>(cap, 1));
   if (int rc = make_map_2d(tx16, xr, xt, 2, ka, rows, ka * 2, kP2BK, 16, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
   return make_map_2d(tx128, xr, xt, 2, ka, rows, ka * 2, kP2BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// --- routed GEMMs on the block-scaled tensor cores (gemm_mx8.cuh) -----------
+// Route chunk of the mx8 kernel: 32 routes (7-stage ring) while the average
+// expert receives fewer than kMx8WideRoutesPerExpert routes, else 128
+// (3-stage ring; each weight tile serves up to 128 routes).
+constexpr int64_t kMx8WideRoutesPerExpert = 48;
+int mx8_bn(int64_t routes, int num_experts) {
+  return routes >= kMx8WideRoutesPerExpert * static_cast<int64_t>(num_experts) ? 128 : 32;
+}
+// The weights reach shared memory by TMA of the 16U4_ALIGN16B type (32-byte
+// aligned base) and their scale words by 4-byte cp.async.
+bool mx8_weights_ok(const void* w, const void* w_scales) { return aligned(w, 32) && aligned(w_scales, 4); }
+
+struct Mx8Act {
+  uint8_t* xh;   // [rows, k] E4M3, routed order
+  uint8_t* xl;
+  uint8_t* sfh;  // [chunk][k/128][512] E8M0
+  uint8_t* sfl;
+};
+size_t mx8_act_bytes(int64_t rows, int64_t k, int64_t max_chunks) {
+  rows = std::max<int64_t>(rows, 1);
+  return 2 * align_up(static_cast<size_t>(rows) * k, 256) +
+         2 * align_up(static_cast<size_t>(std::max<int64_t>(max_chunks, 1)) * (k / 128) * 512, 256);
+}
+Mx8Act carve_mx8_act(uint8_t*& ws, int64_t rows, int64_t k, int64_t max_chunks) {
+  rows = std::max<int64_t>(rows, 1);
+  Mx8Act a;
+  const size_t xb = align_up(static_cast<size_t>(rows) * k, 256);
+  const size_t sb = align_up(static_cast<size_t>(std::max<int64_t>(max_chunks, 1)) * (k / 128) * 512, 256);
+  a.xh = ws;
+  a.xl = ws + xb;
+  a.sfh = ws + 2 * xb;
+  a.sfl = ws + 2 * xb + sb;
+  ws += 2 * xb + 2 * sb;
+  return a;
+}
+
+// Split BF16 rows (gathered in routed order when `sorted` is given) into the
+// mx8 operand, chunk by chunk of the routing's chunk table.
+int run_mx8_split(const void* x, int64_t ldx, int64_t k, const RtRouting& rt, const int32_t* sorted, int64_t routes,
+                  int top_k, const Mx8Act& a, int sms, cudaStream_t s) {
+  const int64_t blocks = rt.cap / kRtBlock;
+  if (blocks <= 0) return MXFP4_OK;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sms) * 2)));
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  const int mc = static_cast<int>(rt.max_chunks);
+  if (sorted)
+    mx8_split_kernel<true><<<grid, kMx8SplitThreads, 0, s>>>(xs, ldx, static_cast<int>(k), rt.chunks, rt.num_chunks, mc, rt.post,
+                                                sorted, static_cast<int>(routes), top_k, a.xh, a.xl, a.sfh, a.sfl);
+  else
+    mx8_split_kernel<false><<<grid, kMx8SplitThreads, 0, s>>>(xs, ldx, static_cast<int>(k), rt.chunks, rt.num_chunks, mc, rt.post,
+                                                 nullptr, 0, 1, a.xh, a.xl, a.sfh, a.sfl);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+
+// Tensor maps of an mx8 GEMM (layouts at mxfp4_routed_mx8_kernel): the packed
+// weights (every expert's rows) as 4-bit elements expanded to the MMA's
+// 16-byte slots, groups of `group` 128-K stages per copy; hi and lo route
+// tiles of 32 rows.
+int mx8_maps(CUtensorMap* tw, CUtensorMap* txh, CUtensorMap* txl, const void* w, int64_t rows_total, int64_t k,
+             const Mx8Act& a, int64_t rows, int64_t glu_inter, int group) {
+  MX_CHECK(aligned(w, 32) && (k / 2) % 32 == 0, "mx8 weights must be 32-byte aligned with a 32-byte row pitch");
+  const uint64_t kt = static_cast<uint64_t>(k / 128);
+  const uint32_t g = static_cast<uint32_t>(group);
+  if (glu_inter > 0) {
+    const uint64_t dims[4] = {128, static_cast<uint64_t>(rows_total), 2, kt};
+    const uint64_t strides[3] = {static_cast<uint64_t>(k / 2), static_cast<uint64_t>(glu_inter * (k / 2)), 64};
+    const uint32_t box[4] = {128, 64, 2, g};
+    if (int rc = make_map_nd(tw, w, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 4, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  } else {
+    const uint64_t dims[3] = {128, static_cast<uint64_t>(rows_total), kt};
+    const uint64_t strides[2] = {static_cast<uint64_t>(k / 2), 64};
+    const uint32_t box[3] = {128, 128, g};
+    if (int rc = make_map_nd(tw, w, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  const uint64_t xdims[3] = {128, static_cast<uint64_t>(std::max<int64_t>(rows, 1)), kt};
+  const uint64_t xstrides[2] = {static_cast<uint64_t>(k), 128};
+  const uint32_t xbox[3] = {128, 32, g};
+  if (int rc = make_map_nd(txh, a.xh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, xdims, xstrides, xbox, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  return make_map_nd(txl, a.xl, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, xdims, xstrides, xbox, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Stages per copy group: 4, 2 or 1, dividing K / 128 (32-route tiles; the
+// 128-route kernel's 3 slots take one stage per copy).
+int mx8_group(int bn, int64_t k) {
+  if (bn == 128) return 1;
+  const int64_t kt = k / 128;
+  return kt % 4 == 0 ? 4 : (kt % 2 == 0 ? 2 : 1);
+}
+
+template <int EPI, int BN>
+int launch_mx8_bn(const CUtensorMap& tw, const CUtensorMap& txh, const CUtensorMap& txl, const Mx8Params& p, int sms,
+                  cudaStream_t stream) {
+  auto kern = mxfp4_routed_mx8_kernel<EPI, BN>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Mx8Cfg<BN>::kSmemBytes);
+  });
+  MX_CUDA(attr_err);
+  const int64_t tiles = static_cast<int64_t>(p.max_chunks) * p.num_wblocks;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms)));
+  kern<<<grid, 256, Mx8Cfg<BN>::kSmemBytes, stream>>>(tw, txh, txl, p);
+  MX_CUDA(cudaGetLastError());
+  return MXFP4_OK;
+}
+template <int EPI>
+int launch_mx8(int bn, const CUtensorMap& tw, const CUtensorMap& txh, const CUtensorMap& txl, const Mx8Params& p,
+               int sms, cudaStream_t stream) {
+  if (bn == 128) return launch_mx8_bn<EPI, 128>(tw, txh, txl, p, sms, stream);
+  return launch_mx8_bn<EPI, 32>(tw, txh, txl, p, sms, stream);
 }
 
 }  // namespace
@@ -1044,6 +1192,10 @@ bool moe_pair_path(int64_t routes, int num_experts) {
 // op's FP32-precision mode with F16/F32 activations (split BF16 parts) keeps
 // the grouped GEMMs.
 bool moe_gemv_path(int64_t routes, const MoeCompute& mc) { return routes <= kMoeGemvMaxRoutes && mc.parts == 1; }
+// Above that and below kPairRoutesPerExpert routes per expert, calls with a
+// BF16 result run the block-scaled grouped GEMM (gemm_mx8.cuh) when the
+// weights' alignment allows it: no weight decode.
+bool mx8_dtypes(int c_dtype) { return c_dtype == MXFP4_DTYPE_BF16; }
 
 // Routing of the pair path: 256-route blocks, no chunk table.
 struct PairRouting {
@@ -1117,6 +1269,15 @@ size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_exp
   size_t b = pair ? pair_routing_bytes(routes, num_experts) : rt_routing_bytes(routes, num_experts);
   if (a_dtype != mc.dtype || mc.parts > 1) b += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
   b += align_up(static_cast<size_t>(std::max<int64_t>(cap, 1)) * ka * 2, 256);  // activations in routed order
+  if (mx8_dtypes(c_dtype) && !pair) {
+    // the mx8 path (taken when the weights' alignment allows it): routing with
+    // its chunk size, converted A, the split activations in routed order
+    size_t m = rt_routing_bytes(routes, num_experts, mx8_bn(routes, num_experts));
+    if (a_dtype != mc.dtype) m += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
+    m += mx8_act_bytes(route_capacity(routes, num_experts, kRtBlock), k,
+                       rt_max_chunks(routes, num_experts, mx8_bn(routes, num_experts)));
+    b = std::max(b, m);
+  }
   return b;
 }
 
@@ -1185,6 +1346,47 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
     g.mul_w = mul_routed_weight ? 1 : 0;
     if (cdt == MXFP4_DTYPE_F16) return launch_moe_gemv<EPI_MOE, true>(g, s);
     return launch_moe_gemv<EPI_MOE, false>(g, s);
+  }
+  if (mx8_dtypes(c_dtype) && !moe_pair_path(routes, num_experts) && mx8_weights_ok(B, B_mx_scale)) {
+    const int bn = mx8_bn(routes, num_experts);
+    const RtRouting rt = carve_rt_routing(ws, routes, num_experts, bn);
+    const void* a_eff;
+    if (int rc = convert_activations(A, a_dtype, a_mx_scale, mc, num_tokens, k, ws, info, s, stream, a_eff)) return rc;
+    MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
+    if (a_eff != A) ws += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
+    if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
+    const Mx8Act act = carve_mx8_act(ws, rt.cap, k, rt.max_chunks);
+    if (int rc = run_mx8_split(a_eff, k, k, rt, rt.sorted, routes, top_k, act, info.sms, s)) return rc;
+    CUtensorMap tw, txh, txl;
+    const int group = mx8_group(bn, k);
+    if (int rc = mx8_maps(&tw, &txh, &txl, B, static_cast<int64_t>(num_experts) * n, k, act, rt.cap, 0, group))
+      return rc;
+    Mx8Params p{};
+    p.group = group;
+    p.N = static_cast<int>(n);
+    p.K = static_cast<int>(k);
+    p.num_wblocks = static_cast<int>((n + 127) / 128);
+    p.w_scales = static_cast<const uint8_t*>(B_mx_scale);
+    p.lds = k / 32;
+    p.w_rows_per_expert = n;
+    p.sfh = act.sfh;
+    p.sfl = act.sfl;
+    p.chunks = rt.chunks;
+    p.num_chunks = rt.num_chunks;
+    p.max_chunks = static_cast<int>(rt.max_chunks);
+    p.sorted_ids = rt.sorted;
+    p.num_routes = static_cast<int>(routes);
+    p.top_k = top_k;
+    p.out = C;
+    p.out_dtype = c_dtype;
+    p.a_scale = a_scale;
+    p.b_scale = b_scale;
+    p.topk_w = topk_weights;
+    p.w_dtype = w_dtype;
+    p.mul_w = mul_routed_weight ? 1 : 0;
+    p.c_stride_t = static_cast<int64_t>(top_k) * n;
+    p.c_stride_j = n;
+    return launch_mx8<EPI_MOE>(bn, tw, txh, txl, p, info.sms, s);
   }
   if (moe_pair_path(routes, num_experts)) {
     // many routes per expert: the pair kernel over 256-route blocks
@@ -1416,6 +1618,17 @@ size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_exp
   b += align_up(static_cast<size_t>(cap) * inter * 2, 256);                           // h in routed order
   b += align_up(static_cast<size_t>(std::max<int64_t>(routes, 1)) * hidden * 2, 256);  // weighted down rows
   b += align_up(static_cast<size_t>(cap) * hidden * 2, 256);                          // x in routed order
+  if (!pair) {
+    // the mx8 path (taken when the weights' alignment allows it)
+    const int bn = mx8_bn(routes, num_experts);
+    const int64_t rcap = std::max<int64_t>(route_capacity(routes, num_experts, kRtBlock), 1);
+    size_t m = rt_routing_bytes(routes, num_experts, bn);
+    m += align_up(static_cast<size_t>(rcap) * inter * 2, 256);                          // h in routed order
+    m += align_up(static_cast<size_t>(std::max<int64_t>(routes, 1)) * hidden * 2, 256);  // weighted down rows
+    const int64_t mch = rt_max_chunks(routes, num_experts, bn);
+    m += mx8_act_bytes(rcap, hidden, mch) + mx8_act_bytes(rcap, inter, mch);            // split x and h
+    b = std::max(b, m);
+  }
   return b;
 }
 
@@ -1489,6 +1702,80 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
     d.w_dtype = w_dtype;
     d.mul_w = 1;
     if (int rc = launch_moe_gemv<EPI_MOE, false>(d, s)) return rc;
+  } else if (!moe_pair_path(routes, num_experts) && mx8_weights_ok(w13, w13_scale) && mx8_weights_ok(w2, w2_scale)) {
+    // block-scaled grouped GEMMs: x and h split into E4M3 hi/lo in routed order
+    const int bn = mx8_bn(routes, num_experts);
+    const RtRouting rt = carve_rt_routing(ws, routes, num_experts, bn);
+    const int64_t cap = std::max<int64_t>(rt.cap, 1);
+    void* hbuf = ws;
+    ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
+    ybuf = ws;
+    ws += align_up(static_cast<size_t>(routes) * hidden * 2, 256);
+    const Mx8Act ax = carve_mx8_act(ws, cap, hidden, rt.max_chunks);
+    const Mx8Act ah = carve_mx8_act(ws, cap, inter, rt.max_chunks);
+    if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
+    if (int rc = run_mx8_split(x, hidden, hidden, rt, rt.sorted, routes, top_k, ax, info.sms, s)) return rc;
+    // gate_up with fused SiLU(gate) * up -> h [cap, inter] in routed order
+    {
+      CUtensorMap tw, txh, txl;
+      const int group = mx8_group(bn, hidden);
+      if (int rc = mx8_maps(&tw, &txh, &txl, w13, static_cast<int64_t>(num_experts) * 2 * inter, hidden, ax, cap, inter,
+                            group))
+        return rc;
+      Mx8Params p{};
+      p.group = group;
+      p.N = static_cast<int>(2 * inter);
+      p.glu_inter = static_cast<int>(inter);
+      p.K = static_cast<int>(hidden);
+      p.num_wblocks = static_cast<int>((inter + 63) / 64);
+      p.w_scales = static_cast<const uint8_t*>(w13_scale);
+      p.lds = hidden / 32;
+      p.w_rows_per_expert = 2 * inter;
+      p.sfh = ax.sfh;
+      p.sfl = ax.sfl;
+      p.chunks = rt.chunks;
+      p.num_chunks = rt.num_chunks;
+      p.max_chunks = static_cast<int>(rt.max_chunks);
+      p.sorted_ids = rt.sorted;
+      p.num_routes = static_cast<int>(routes);
+      p.top_k = top_k;
+      p.out = hbuf;
+      p.ldo = inter;
+      p.out_dtype = MXFP4_DTYPE_BF16;
+      if (int rc = launch_mx8<EPI_GLU>(bn, tw, txh, txl, p, info.sms, s)) return rc;
+    }
+    if (int rc = run_mx8_split(hbuf, inter, inter, rt, nullptr, routes, 1, ah, info.sms, s)) return rc;
+    // down with route weights, scattered to y[route]
+    {
+      CUtensorMap tw, txh, txl;
+      const int group = mx8_group(bn, inter);
+      if (int rc = mx8_maps(&tw, &txh, &txl, w2, static_cast<int64_t>(num_experts) * hidden, inter, ah, cap, 0, group))
+        return rc;
+      Mx8Params p{};
+      p.group = group;
+      p.N = static_cast<int>(hidden);
+      p.K = static_cast<int>(inter);
+      p.num_wblocks = static_cast<int>((hidden + 127) / 128);
+      p.w_scales = static_cast<const uint8_t*>(w2_scale);
+      p.lds = inter / 32;
+      p.w_rows_per_expert = hidden;
+      p.sfh = ah.sfh;
+      p.sfl = ah.sfl;
+      p.chunks = rt.chunks;
+      p.num_chunks = rt.num_chunks;
+      p.max_chunks = static_cast<int>(rt.max_chunks);
+      p.sorted_ids = rt.sorted;
+      p.num_routes = static_cast<int>(routes);
+      p.top_k = 1;
+      p.out = ybuf;
+      p.out_dtype = MXFP4_DTYPE_BF16;
+      p.topk_w = topk_weights;
+      p.w_dtype = w_dtype;
+      p.mul_w = 1;
+      p.c_stride_t = hidden;
+      p.c_stride_j = 0;
+      if (int rc = launch_mx8<EPI_MOE>(bn, tw, txh, txl, p, info.sms, s)) return rc;
+    }
   } else if (moe_pair_path(routes, num_experts)) {
     // many routes per expert: pair kernel over 256-route blocks
     const PairRouting pr = carve_pair_routing(ws, routes, num_experts);
