@@ -493,7 +493,8 @@ size_t mx8_act_bytes(int64_t rows, int64_t k, int64_t max_chunks) {
   return 2 * align_up(static_cast<size_t>(rows) * k, 256) +
          2 * align_up(static_cast<size_t>(std::max<int64_t>(max_chunks, 1)) * (k / 128) * 512, 256);
 }
-Mx8Act carve_mx8_act(uint8_t*& ws, int64_t rows, int64_t k, int64_t max_chunks) {
+// 32-route chunks keep lo's scales in the hi chunk's second column (sfl = sfh + 4).
+Mx8Act carve_mx8_act(uint8_t*& ws, int64_t rows, int64_t k, int64_t max_chunks, int bn) {
   rows = std::max<int64_t>(rows, 1);
   Mx8Act a;
   const size_t xb = align_up(static_cast<size_t>(rows) * k, 256);
@@ -501,7 +502,7 @@ Mx8Act carve_mx8_act(uint8_t*& ws, int64_t rows, int64_t k, int64_t max_chunks) 
   a.xh = ws;
   a.xl = ws + xb;
   a.sfh = ws + 2 * xb;
-  a.sfl = ws + 2 * xb + sb;
+  a.sfl = bn == 32 ? a.sfh + 4 : ws + 2 * xb + sb;
   ws += 2 * xb + 2 * sb;
   return a;
 }
@@ -530,7 +531,7 @@ int run_mx8_split(const void* x, int64_t ldx, int64_t k, const RtRouting& rt, co
 // 16-byte slots, groups of `group` 128-K stages per copy; hi and lo route
 // tiles of 32 rows.
 int mx8_maps(CUtensorMap* tw, CUtensorMap* txh, CUtensorMap* txl, const void* w, int64_t rows_total, int64_t k,
-             const Mx8Act& a, int64_t rows, int64_t glu_inter, int group) {
+             const Mx8Act& a, int64_t rows, int64_t glu_inter, int group, int bn) {
   MX_CHECK(aligned(w, 32) && (k / 2) % 32 == 0, "mx8 weights must be 32-byte aligned with a 32-byte row pitch");
   const uint64_t kt = static_cast<uint64_t>(k / 128);
   const uint32_t g = static_cast<uint32_t>(group);
@@ -548,6 +549,14 @@ int mx8_maps(CUtensorMap* tw, CUtensorMap* txh, CUtensorMap* txl, const void* w,
     if (int rc = make_map_nd(tw, w, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, dims, strides, box,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
+  }
+  if (bn == 32) {
+    // hi and lo as one tensor: the part dimension steps from xh to xl
+    const uint64_t xdims[4] = {128, static_cast<uint64_t>(std::max<int64_t>(rows, 1)), 2, kt};
+    const uint64_t xstrides[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(a.xl - a.xh), 128};
+    const uint32_t xbox[4] = {128, 32, 2, g};
+    *txl = {};
+    return make_map_nd(txh, a.xh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, xdims, xstrides, xbox, CU_TENSOR_MAP_SWIZZLE_128B);
   }
   const uint64_t xdims[3] = {128, static_cast<uint64_t>(std::max<int64_t>(rows, 1)), kt};
   const uint64_t xstrides[2] = {static_cast<uint64_t>(k), 128};
@@ -1355,11 +1364,11 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
     MX_CHECK(aligned(a_eff, 16), "A must be 16-byte aligned");
     if (a_eff != A) ws += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
     if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
-    const Mx8Act act = carve_mx8_act(ws, rt.cap, k, rt.max_chunks);
+    const Mx8Act act = carve_mx8_act(ws, rt.cap, k, rt.max_chunks, bn);
     if (int rc = run_mx8_split(a_eff, k, k, rt, rt.sorted, routes, top_k, act, info.sms, s)) return rc;
     CUtensorMap tw, txh, txl;
     const int group = mx8_group(bn, k);
-    if (int rc = mx8_maps(&tw, &txh, &txl, B, static_cast<int64_t>(num_experts) * n, k, act, rt.cap, 0, group))
+    if (int rc = mx8_maps(&tw, &txh, &txl, B, static_cast<int64_t>(num_experts) * n, k, act, rt.cap, 0, group, bn))
       return rc;
     Mx8Params p{};
     p.group = group;
@@ -1711,8 +1720,8 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
     ws += align_up(static_cast<size_t>(cap) * inter * 2, 256);
     ybuf = ws;
     ws += align_up(static_cast<size_t>(routes) * hidden * 2, 256);
-    const Mx8Act ax = carve_mx8_act(ws, cap, hidden, rt.max_chunks);
-    const Mx8Act ah = carve_mx8_act(ws, cap, inter, rt.max_chunks);
+    const Mx8Act ax = carve_mx8_act(ws, cap, hidden, rt.max_chunks, bn);
+    const Mx8Act ah = carve_mx8_act(ws, cap, inter, rt.max_chunks, bn);
     if (int rc = run_rt_routing(topk_ids, ids_dtype, routes, num_experts, rt, s)) return rc;
     if (int rc = run_mx8_split(x, hidden, hidden, rt, rt.sorted, routes, top_k, ax, info.sms, s)) return rc;
     // gate_up with fused SiLU(gate) * up -> h [cap, inter] in routed order
@@ -1720,7 +1729,7 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
       CUtensorMap tw, txh, txl;
       const int group = mx8_group(bn, hidden);
       if (int rc = mx8_maps(&tw, &txh, &txl, w13, static_cast<int64_t>(num_experts) * 2 * inter, hidden, ax, cap, inter,
-                            group))
+                            group, bn))
         return rc;
       Mx8Params p{};
       p.group = group;
@@ -1749,7 +1758,7 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
     {
       CUtensorMap tw, txh, txl;
       const int group = mx8_group(bn, inter);
-      if (int rc = mx8_maps(&tw, &txh, &txl, w2, static_cast<int64_t>(num_experts) * hidden, inter, ah, cap, 0, group))
+      if (int rc = mx8_maps(&tw, &txh, &txl, w2, static_cast<int64_t>(num_experts) * hidden, inter, ah, cap, 0, group, bn))
         return rc;
       Mx8Params p{};
       p.group = group;

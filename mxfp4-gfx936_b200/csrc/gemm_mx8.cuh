@@ -44,7 +44,8 @@
 //            = 4 codes per row and stage) by 4-byte cp.async into the
 //            512-byte chunk layout
 //   warp 1   MMA issuer: tcgen05.cp of the stage's scales into its tensor
-//            memory region, then per 32 K two MMAs (hi, lo)
+//            memory region, then per 32 K one MMA over the hi and lo rows
+//            stacked along N (32-route tiles) or two MMAs, hi and lo
 //   warps 4-7 epilogue, one per tensor-memory lane quarter (the routed
 //            kernels' epilogue: GLU, or the routed op's rounding chain)
 // Two accumulators of BN columns alternate between tiles, so a tile's
@@ -64,22 +65,26 @@ struct Mx8Cfg {
   // (G = 4, 2 or 1, dividing both the slot count and K / 128) with one copy
   // per operand, so copies are few and large
   static constexpr int kSlots = BN == 128 ? 3 : 8;
-  // independent accumulators per tile (summed by the epilogue): hi/lo x
-  // even/odd K steps for 32-route tiles
+  // accumulator pieces per tile, summed by the epilogue: 32-route tiles keep
+  // even and odd K steps apart (independent MMA chains), each as hi then lo
+  // columns: hi even, lo even, hi odd, lo odd, BN columns apart
   static constexpr int kAcc = BN == 32 ? 4 : 1;
   static_assert(kAcc * BN <= 128, "accumulator slot");
   static constexpr int kABytes = 128 * 128;          // 128 weight rows x 128 K (one byte per code in shared memory)
-  static constexpr int kBBytes = BN * 128;           // BN routes x 128 K, E4M3
+  static constexpr int kBBytes = BN * 128;           // BN routes x 128 K, E4M3 (hi; lo right after it)
+  // 32-route tiles stack hi and lo along the MMA's N (one N = 64 MMA per
+  // 32 K, the scales of both in one chunk: hi in column 0, lo in column 1);
+  // 128-route tiles take two N = 128 MMAs (hi, lo) per 32 K
+  static constexpr bool kStackHiLo = BN == 32;
   static constexpr int kSfaBytes = 512;
   static constexpr int kSfbBytes = 512;              // one route chunk (up to 128 routes)
   static constexpr int kOutBytes = BN * 128 * 2;     // staging: BN routes x 128 features, 16-bit outputs
   static constexpr int kOffA = 0;
-  static constexpr int kOffBh = kOffA + kSlots * kABytes;
-  static constexpr int kOffBl = kOffBh + kSlots * kBBytes;
-  static constexpr int kOffSfa = kOffBl + kSlots * kBBytes;
-  static constexpr int kOffSfbh = kOffSfa + kSlots * kSfaBytes;
-  static constexpr int kOffSfbl = kOffSfbh + kSlots * kSfbBytes;
-  static constexpr int kOffOut = kOffSfbl + kSlots * kSfbBytes;
+  static constexpr int kOffB = kOffA + kSlots * kABytes;          // per slot: hi tile, lo tile
+  static constexpr int kOffSfa = kOffB + kSlots * 2 * kBBytes;
+  static constexpr int kOffSfb = kOffSfa + kSlots * kSfaBytes;    // per slot: hi chunk (+ lo chunk)
+  static constexpr int kSfbSlot = kStackHiLo ? kSfbBytes : 2 * kSfbBytes;
+  static constexpr int kOffOut = kOffSfb + kSlots * kSfbSlot;
   static constexpr int kOffRoute = kOffOut + kOutBytes;       // BN route ids + BN route weights
   static constexpr int kOffVote = kOffRoute + BN * 8;
   static constexpr int kOffBar = kOffVote + 16;
@@ -105,8 +110,8 @@ struct Mx8Params {
   const uint8_t* w_scales;      // [E * rows, K / 32]
   int64_t lds;
   int64_t w_rows_per_expert;
-  const uint8_t* sfh;           // activation scales [chunk][K/128][512] (hi, lo)
-  const uint8_t* sfl;
+  const uint8_t* sfh;           // activation scales [chunk][K/128][512]: hi (32-route tiles: hi and lo)
+  const uint8_t* sfl;           // lo (128-route tiles)
   const int4* chunks;           // {first routed row, rows, expert, 0}
   const int32_t* num_chunks;
   int max_chunks;
@@ -148,6 +153,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
 __device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
@@ -246,6 +259,7 @@ __global__ void __launch_bounds__(kMx8SplitThreads) mx8_split_kernel(const uint1
                                                          int top_k, uint8_t* __restrict__ xh,
                                                          uint8_t* __restrict__ xl, uint8_t* __restrict__ sfh,
                                                          uint8_t* __restrict__ sfl) {
+  // sfl == sfh + 4: lo's scales in the chunk's next 32-row column (32-route chunks)
   __shared__ int s_chunk[2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   int nch = num_chunks[0];
@@ -345,8 +359,11 @@ __device__ __forceinline__ void mx8_load_acc(uint32_t taddr, uint32_t (&r)[32]) 
 // {128 K, rows, 2 halves (inter rows apart), K / 128 stages}, box
 // {128, 64, 2, group}.  Either way a group of stages of the 128-row A tile
 // (GLU: the 64 gate rows then the 64 up rows of the same columns) lands as
-// [stage][128 rows][128 bytes].  Route maps (tmap_xh / tmap_xl): 3-D over the
-// E4M3 rows, dims {128 K, rows, K / 128 stages}, box {128, 32, group}.
+// [stage][128 rows][128 bytes].  Route maps over the E4M3 rows: 32-route tiles
+// one 4-D map (tmap_xh), dims {128 K, rows, 2 parts (hi, lo), K / 128 stages},
+// box {128, 32, 2, group}, landing as [stage][hi 32 rows, lo 32 rows];
+// 128-route tiles 3-D maps of hi (tmap_xh) and lo (tmap_xl), dims
+// {128 K, rows, K / 128 stages}, box {128, 32, 1}.
 template <int EPI, int BN>
 __global__ void __launch_bounds__(256, 1)
     mxfp4_routed_mx8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_xh,
@@ -375,7 +392,7 @@ __global__ void __launch_bounds__(256, 1)
   // the group shape and the 16-bit output the staging tile is sized for,
   // checked before any copy is issued; the host establishes them, so this only
   // guards against a caller that bypassed its checks
-  if ((reinterpret_cast<uintptr_t>(p.sfh) & 15) != 0 || (reinterpret_cast<uintptr_t>(p.sfl) & 15) != 0 ||
+  if ((reinterpret_cast<uintptr_t>(p.sfh) & 15) != 0 || (!Cfg::kStackHiLo && (reinterpret_cast<uintptr_t>(p.sfl) & 15) != 0) ||
       (reinterpret_cast<uintptr_t>(p.w_scales) & 3) != 0 || (p.lds & 3) != 0 || (p.K & 127) != 0 ||
       p.out_dtype == MXFP4_DTYPE_F32 || G < 1 || S % G != 0 || KT % G != 0) {
     if (threadIdx.x == 0) record_error(MXFP4_ERR_INVALID_ARGUMENT);
@@ -398,7 +415,7 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_xh);
-    prefetch_tmap(&tmap_xl);
+    if (!Cfg::kStackHiLo) prefetch_tmap(&tmap_xl);  // unused (zero) with stacked hi/lo
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kMx8TmemCols);
@@ -426,7 +443,7 @@ __global__ void __launch_bounds__(256, 1)
         bool v;
         const int row0 = static_cast<int>(mx8_weight_row<EPI>(p, ch.z, wb, 0, v));
         const int nbox = ch.y / 32;  // one box when G > 1 (BN = 32)
-        const uint32_t tx = G * (128 * 64 + 2 * ch.y * 128 + 2 * Cfg::kSfbBytes);
+        const uint32_t tx = G * (128 * 64 + 2 * ch.y * 128 + Cfg::kSfbSlot);
         for (int kg = 0; kg < KG; ++kg, ++it) {
           const int g = it % NG;
           const uint32_t ph = (it / NG) & 1;
@@ -439,13 +456,20 @@ __global__ void __launch_bounds__(256, 1)
             tma_load_4d_hint(smem + Cfg::kOffA + s0 * Cfg::kABytes, &tmap_w, &full[g], 0, row0, 0, kt0, pol_w);
           else
             tma_load_3d_hint(smem + Cfg::kOffA + s0 * Cfg::kABytes, &tmap_w, &full[g], 0, row0, kt0, pol_w);
-          for (int i = 0; i < nbox; ++i) {
-            tma_load_3d(smem + Cfg::kOffBh + s0 * Cfg::kBBytes + i * 32 * 128, &tmap_xh, &full[g], 0, ch.x + 32 * i, kt0);
-            tma_load_3d(smem + Cfg::kOffBl + s0 * Cfg::kBBytes + i * 32 * 128, &tmap_xl, &full[g], 0, ch.x + 32 * i, kt0);
-          }
+          uint8_t* bslot = smem + Cfg::kOffB + s0 * 2 * Cfg::kBBytes;
           const int64_t sfo = (static_cast<int64_t>(ci) * KT + kt0) * 512;
-          bulk_load(smem + Cfg::kOffSfbh + s0 * Cfg::kSfbBytes, p.sfh + sfo, G * Cfg::kSfbBytes, &full[g]);
-          bulk_load(smem + Cfg::kOffSfbl + s0 * Cfg::kSfbBytes, p.sfl + sfo, G * Cfg::kSfbBytes, &full[g]);
+          if (Cfg::kStackHiLo) {
+            // [stage][hi 32 rows, lo 32 rows] in one copy; the scales of both in one chunk per stage
+            tma_load_4d(bslot, &tmap_xh, &full[g], 0, ch.x, 0, kt0);
+            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot, p.sfh + sfo, G * Cfg::kSfbBytes, &full[g]);
+          } else {
+            for (int i = 0; i < nbox; ++i) {
+              tma_load_3d(bslot + i * 32 * 128, &tmap_xh, &full[g], 0, ch.x + 32 * i, kt0);
+              tma_load_3d(bslot + Cfg::kBBytes + i * 32 * 128, &tmap_xl, &full[g], 0, ch.x + 32 * i, kt0);
+            }
+            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot, p.sfh + sfo, Cfg::kSfbBytes, &full[g]);
+            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot + Cfg::kSfbBytes, p.sfl + sfo, Cfg::kSfbBytes, &full[g]);
+          }
         }
       }
       if (!ok || *abort_flag)
@@ -496,7 +520,7 @@ __global__ void __launch_bounds__(256, 1)
       bool ok = true, issued = false;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tl) {
         const int4 ch = p.chunks[t / p.num_wblocks];
-        const uint32_t idesc0 = idesc_mx8(128, ch.y);
+        const uint32_t idesc0 = idesc_mx8(128, Cfg::kStackHiLo ? 2 * ch.y : ch.y);
         const int acc = tl & 1;
         if (!mbar_wait(&tempty[acc], ((tl >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
@@ -511,20 +535,21 @@ __global__ void __launch_bounds__(256, 1)
             const int kt = kg * G + st;
             const uint32_t sf_t = tmem_base + kMx8SfCol + kMx8SfRegion * s;  // weights, hi, lo: 4 columns each
             tmem_cp_32x128b_warpx4(sf_t, desc_sf_chunk(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
-            tmem_cp_32x128b_warpx4(sf_t + 4, desc_sf_chunk(smem_u32(smem + Cfg::kOffSfbh + s * Cfg::kSfbBytes)));
-            tmem_cp_32x128b_warpx4(sf_t + 8, desc_sf_chunk(smem_u32(smem + Cfg::kOffSfbl + s * Cfg::kSfbBytes)));
+            const uint32_t sfb_smem = smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbSlot);
+            tmem_cp_32x128b_warpx4(sf_t + 4, desc_sf_chunk(sfb_smem));
+            if (!Cfg::kStackHiLo) tmem_cp_32x128b_warpx4(sf_t + 8, desc_sf_chunk(sfb_smem + Cfg::kSfbBytes));
             const uint64_t adesc = desc_sw128(smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes));
-            const uint64_t bhdesc = desc_sw128(smem_u32(smem + Cfg::kOffBh + s * Cfg::kBBytes));
-            const uint64_t bldesc = desc_sw128(smem_u32(smem + Cfg::kOffBl + s * Cfg::kBBytes));
+            const uint64_t bhdesc = desc_sw128(smem_u32(smem + Cfg::kOffB + s * 2 * Cfg::kBBytes));
+            const uint64_t bldesc = desc_sw128(smem_u32(smem + Cfg::kOffB + s * 2 * Cfg::kBBytes + Cfg::kBBytes));
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t sel = static_cast<uint32_t>(j) << 30;
               const uint32_t idesc = idesc0 | (static_cast<uint32_t>(j) << 29) | (static_cast<uint32_t>(j) << 4);
-              if (Cfg::kAcc == 4) {
-                const uint32_t dh = d_tmem + (j & 1) * 2 * BN;
+              if (Cfg::kStackHiLo) {
+                // N = hi rows then lo rows: columns [0, 32) hi, [32, 64) lo of the even / odd K-step accumulator
                 const uint32_t first = (kt == 0 && j < 2) ? 0u : 1u;
-                umma_mx8(dh, adesc + 2 * j, bhdesc + 2 * j, idesc, sf_t | sel, (sf_t + 4) | sel, first);
-                umma_mx8(dh + BN, adesc + 2 * j, bldesc + 2 * j, idesc, sf_t | sel, (sf_t + 8) | sel, first);
+                umma_mx8(d_tmem + (j & 1) * 2 * BN, adesc + 2 * j, bhdesc + 2 * j, idesc, sf_t | sel, (sf_t + 4) | sel,
+                         first);
               } else {
                 umma_mx8(d_tmem, adesc + 2 * j, bhdesc + 2 * j, idesc, sf_t | sel, (sf_t + 4) | sel, (kt | j) != 0);
                 umma_mx8(d_tmem, adesc + 2 * j, bldesc + 2 * j, idesc, sf_t | sel, (sf_t + 8) | sel, 1);
