@@ -488,12 +488,14 @@ struct Mx8Act {
   uint8_t* sfh;  // [chunk][k/128][512] E8M0
   uint8_t* sfl;
 };
-size_t mx8_act_bytes(int64_t rows, int64_t k, int64_t max_chunks) {
+// Bytes of the split activations: hi and lo rows, and the scale chunks --
+// one array for 32-route chunks (lo's scales in the hi chunk's second column,
+// sfl = sfh + 4), a hi and a lo array for 128-route chunks.
+size_t mx8_act_bytes(int64_t rows, int64_t k, int64_t max_chunks, int bn) {
   rows = std::max<int64_t>(rows, 1);
-  return 2 * align_up(static_cast<size_t>(rows) * k, 256) +
-         2 * align_up(static_cast<size_t>(std::max<int64_t>(max_chunks, 1)) * (k / 128) * 512, 256);
+  const size_t sb = align_up(static_cast<size_t>(std::max<int64_t>(max_chunks, 1)) * (k / 128) * 512, 256);
+  return 2 * align_up(static_cast<size_t>(rows) * k, 256) + (bn == 32 ? 1 : 2) * sb;
 }
-// 32-route chunks keep lo's scales in the hi chunk's second column (sfl = sfh + 4).
 Mx8Act carve_mx8_act(uint8_t*& ws, int64_t rows, int64_t k, int64_t max_chunks, int bn) {
   rows = std::max<int64_t>(rows, 1);
   Mx8Act a;
@@ -503,7 +505,7 @@ Mx8Act carve_mx8_act(uint8_t*& ws, int64_t rows, int64_t k, int64_t max_chunks, 
   a.xl = ws + xb;
   a.sfh = ws + 2 * xb;
   a.sfl = bn == 32 ? a.sfh + 4 : ws + 2 * xb + sb;
-  ws += 2 * xb + 2 * sb;
+  ws += 2 * xb + (bn == 32 ? 1 : 2) * sb;
   return a;
 }
 
@@ -1281,10 +1283,10 @@ size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_exp
   if (mx8_dtypes(c_dtype) && !pair) {
     // the mx8 path (taken when the weights' alignment allows it): routing with
     // its chunk size, converted A, the split activations in routed order
-    size_t m = rt_routing_bytes(routes, num_experts, mx8_bn(routes, num_experts));
+    const int bn = mx8_bn(routes, num_experts);
+    size_t m = rt_routing_bytes(routes, num_experts, bn);
     if (a_dtype != mc.dtype) m += align_up(static_cast<size_t>(num_tokens) * k * 2, 256);
-    m += mx8_act_bytes(route_capacity(routes, num_experts, kRtBlock), k,
-                       rt_max_chunks(routes, num_experts, mx8_bn(routes, num_experts)));
+    m += mx8_act_bytes(route_capacity(routes, num_experts, kRtBlock), k, rt_max_chunks(routes, num_experts, bn), bn);
     b = std::max(b, m);
   }
   return b;
@@ -1635,7 +1637,7 @@ size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_exp
     m += align_up(static_cast<size_t>(rcap) * inter * 2, 256);                          // h in routed order
     m += align_up(static_cast<size_t>(std::max<int64_t>(routes, 1)) * hidden * 2, 256);  // weighted down rows
     const int64_t mch = rt_max_chunks(routes, num_experts, bn);
-    m += mx8_act_bytes(rcap, hidden, mch) + mx8_act_bytes(rcap, inter, mch);            // split x and h
+    m += mx8_act_bytes(rcap, hidden, mch, bn) + mx8_act_bytes(rcap, inter, mch, bn);    // split x and h
     b = std::max(b, m);
   }
   return b;

@@ -62,7 +62,18 @@ def _worker(rank, world, port, q):
                 ys = soft.linear_mxfp4_soft(xm, w, s)
                 fused_ok = fused_ok and bool(torch.equal(yf.view(torch.int16), ys.view(torch.int16)))
         lin_ok = lin_ok and fused_ok
-        # expert-parallel MoE: every rank owns its tokens and E/world experts
+        # expert-parallel MoE: every rank owns its tokens and E/world experts.
+        # The owners' grouped GEMMs (BF16 tensor cores) and the one-GPU layer
+        # (block-scaled E2M1 x E4M3 kernel below 128 routes per expert) sum
+        # the same exact products in different orders: compared within the
+        # operator tolerance (2 BF16 ulps of the largest output, 1e-3
+        # relative Frobenius error) instead of bit for bit
+        def close(a, b):
+            a, b = a.float(), b.float()
+            err = (a - b).abs()
+            ulp = 2.0 ** (torch.floor(torch.log2(b.abs().max())) - 7)
+            return bool(err.max() <= 2 * ulp) and bool(err.norm() <= 1e-3 * b.norm())
+
         t_local, h, e, top_k, inter = 512, 1024, 32, 4, 256
         x_all = torch.randn(world * t_local, h, generator=g, device=dev).to(torch.bfloat16)
         w13 = torch.randint(0, 256, (e, 2 * inter, h // 2), generator=g, device=dev, dtype=torch.uint8)
@@ -75,18 +86,18 @@ def _worker(rank, world, port, q):
         # NCCL all-to-all path
         layer_n = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, fused=False)
         y_n = layer_n(x_all[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous())
-        ep_ok = bool(torch.equal(y_n.view(torch.int16), y_full.view(torch.int16)))
+        ep_ok = close(y_n, y_full)
         # native path (peer-mapped dispatch/combine, device barriers): two calls on
         # the same buffers, the second with new routes and fewer tokens on rank 1
         layer = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world)
         assert layer.fused
         y_ep = layer(x_all[sl].contiguous(), tw[sl].contiguous(), tid[sl].contiguous())
-        ep_ok = ep_ok and bool(torch.equal(y_ep.view(torch.int16), y_full.view(torch.int16)))
+        ep_ok = ep_ok and close(y_ep, y_full)
         tw2, tid2 = torch.topk(torch.softmax(torch.randn(world * t_local, e, generator=g, device=dev), -1), top_k, -1)
         y_full2 = soft.moe_layer_mxfp4(x_all, w13, s13, w2, s2, tw2, tid2)[sl]
         n2 = t_local if rank == 0 else t_local - 100
         y_ep2 = layer(x_all[sl][:n2].contiguous(), tw2[sl][:n2].contiguous(), tid2[sl][:n2].contiguous())
-        ep_ok = ep_ok and bool(torch.equal(y_ep2.view(torch.int16), y_full2[:n2].view(torch.int16)))
+        ep_ok = ep_ok and close(y_ep2, y_full2[:n2])
         # both owner GEMMs: 32-row blocks (routed tensor-memory GEMM) while the
         # ranks' routes average fewer than 128 per local expert, 256-row blocks
         # (CTA-pair GEMM) from there on; world = 1 above is the former, so run
@@ -98,7 +109,7 @@ def _worker(rank, world, port, q):
             y_full3 = soft.moe_layer_mxfp4(x3, w13, s13, w2, s2, tw3, tid3)
             layer3 = ep.ExpertParallelMoE.from_full(w13, s13, w2, s2, rank, world, max_tokens=t3)
             y_ep3 = layer3(x3, tw3.contiguous(), tid3.contiguous())
-            ep_ok = ep_ok and bool(torch.equal(y_ep3.view(torch.int16), y_full3.view(torch.int16)))
+            ep_ok = ep_ok and close(y_ep3, y_full3)
         torch.cuda.synchronize()
         q.put((rank, lin_ok, ep_ok, soft.device_status()))
     finally:
