@@ -394,6 +394,15 @@ def moe_weight_bytes(tid, cfg=MOE):
     return experts * per_expert + 2 * 2 * tid.shape[0] * h
 
 
+def moe_kernel_name(routes, experts):
+    """The grouped GEMM the MoE layer (BF16) runs at this route count."""
+    if routes <= 64:
+        return "routed GEMV"
+    if routes < 128 * experts:
+        return "block-scaled routed GEMM (E2M1 x E4M3 hi/lo, " + ("32" if routes < 48 * experts else "128") + "-route tiles)"
+    return "pair GEMM (256-route blocks)"
+
+
 def bench_moe_decode(soft, device, tokens_list=(1, 8, 64, 256), steps=50, warmup=5):
     """The config-2 layer shape at decode batch sizes (config 4's decode MoE):
     CUDA-graph replays over two input sets with their own weights (426 MB, more
@@ -406,7 +415,7 @@ def bench_moe_decode(soft, device, tokens_list=(1, 8, 64, 256), steps=50, warmup
         ms = bench_moe(soft, steps, warmup, device, tokens=t)
         out[f"t{t}"] = {"us": ms * 1e3, "tokens_per_s": t / (ms * 1e-3), "hbm_bytes": byts,
                         "gbs": byts / ms / 1e6, "frac_hbm": byts / ms / 1e6 / hbm,
-                        "kernel": "routed GEMV" if t * MOE["k"] <= 64 else "tensor-memory routed GEMM"}
+                        "kernel": moe_kernel_name(t * MOE["k"], MOE["e"])}
     return out
 
 

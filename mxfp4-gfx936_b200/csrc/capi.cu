@@ -588,7 +588,7 @@ int launch_mx8_bn(const CUtensorMap& tw, const CUtensorMap& txh, const CUtensorM
   MX_CUDA(attr_err);
   const int64_t tiles = static_cast<int64_t>(p.max_chunks) * p.num_wblocks;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms)));
-  kern<<<grid, 256, Mx8Cfg<BN>::kSmemBytes, stream>>>(tw, txh, txl, p);
+  kern<<<grid, Mx8Cfg<BN>::kThreads, Mx8Cfg<BN>::kSmemBytes, stream>>>(tw, txh, txl, p);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
 }

@@ -43,9 +43,12 @@
 //   warp 2   weight-scale producer: the weights' scale words (one 32-bit word
 //            = 4 codes per row and stage) by 4-byte cp.async into the
 //            512-byte chunk layout
-//   warp 1   MMA issuer: tcgen05.cp of the stage's scales into its tensor
-//            memory region, then per 32 K one MMA over the hi and lo rows
-//            stacked along N (32-route tiles) or two MMAs, hi and lo
+//   warps 8-11 scale writers, one per tensor-memory lane quarter: each
+//            stage's weight and activation scales from shared memory into
+//            the stage's tensor-memory region with tcgen05.st (the per-stage
+//            scale copies kept off the MMA thread)
+//   warp 1   MMA issuer: per 32 K one MMA over the hi and lo rows stacked
+//            along N (32-route tiles) or two MMAs, hi and lo
 //   warps 4-7 epilogue, one per tensor-memory lane quarter (the routed
 //            kernels' epilogue: GLU, or the routed op's rounding chain)
 // Two accumulators of BN columns alternate between tiles, so a tile's
@@ -88,7 +91,8 @@ struct Mx8Cfg {
   static constexpr int kOffRoute = kOffOut + kOutBytes;       // BN route ids + BN route weights
   static constexpr int kOffVote = kOffRoute + BN * 8;
   static constexpr int kOffBar = kOffVote + 16;
-  static constexpr int kNumBars = 2 * kSlots + 5;
+  static constexpr int kNumBars = 3 * kSlots + 5;
+  static constexpr int kThreads = 384;  // warps 0-3 copies / MMA, 4-7 epilogue, 8-11 scale writers
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "mx8 kernel shared memory");
@@ -365,7 +369,7 @@ __device__ __forceinline__ void mx8_load_acc(uint32_t taddr, uint32_t (&r)[32]) 
 // 128-route tiles 3-D maps of hi (tmap_xh) and lo (tmap_xl), dims
 // {128 K, rows, K / 128 stages}, box {128, 32, 1}.
 template <int EPI, int BN>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(Mx8Cfg<BN>::kThreads, 1)
     mxfp4_routed_mx8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_xh,
                             const __grid_constant__ CUtensorMap tmap_xl, const Mx8Params p) {
   using Cfg = Mx8Cfg<BN>;
@@ -378,6 +382,7 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* tfull = empty + S;     // [2]
   uint64_t* tempty = tfull + 2;    // [2]
   uint64_t* drain = tempty + 2;
+  uint64_t* sfready = drain + 1;   // [S]: a group's scales are in tensor memory (4 scale-writer warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
   int32_t* route_ids = reinterpret_cast<int32_t*>(smem + Cfg::kOffRoute);
@@ -409,6 +414,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&tempty[a], 4);
     }
     mbar_init(drain, 1);
+    for (int g = 0; g < S; ++g) mbar_init(&sfready[g], 4);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -528,16 +534,13 @@ __global__ void __launch_bounds__(256, 1)
         for (int kg = 0; kg < KG; ++kg, ++it) {
           const int g = it % NG;
           if (!mbar_wait(&full[g], (it / NG) & 1, abort_flag)) { ok = false; break; }
-          fence_proxy_async();  // the cp.async-written scale words, for tcgen05.cp
+          // the group's scales, written into tensor memory by the scale-writer warps
+          if (!mbar_wait(&sfready[g], (it / NG) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           for (int st = 0; st < G; ++st) {
             const int s = g * G + st;
             const int kt = kg * G + st;
             const uint32_t sf_t = tmem_base + kMx8SfCol + kMx8SfRegion * s;  // weights, hi, lo: 4 columns each
-            tmem_cp_32x128b_warpx4(sf_t, desc_sf_chunk(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
-            const uint32_t sfb_smem = smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbSlot);
-            tmem_cp_32x128b_warpx4(sf_t + 4, desc_sf_chunk(sfb_smem));
-            if (!Cfg::kStackHiLo) tmem_cp_32x128b_warpx4(sf_t + 8, desc_sf_chunk(sfb_smem + Cfg::kSfbBytes));
             const uint64_t adesc = desc_sw128(smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes));
             const uint64_t bhdesc = desc_sw128(smem_u32(smem + Cfg::kOffB + s * 2 * Cfg::kBBytes));
             const uint64_t bldesc = desc_sw128(smem_u32(smem + Cfg::kOffB + s * 2 * Cfg::kBBytes + Cfg::kBBytes));
@@ -569,6 +572,44 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
     __syncwarp();
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------------ scale writers (warps 8-11)
+    // Warp 8 + q writes lane quarter q of each stage's tensor-memory scale
+    // region: lane i takes the 16 bytes of row i of the stage's weight-scale
+    // chunk and of its activation-scale chunk(s) from shared memory (the
+    // layout tcgen05.cp .32x128b.warpx4 would copy: column j = rows 32 j + i,
+    // the same in all four quarters) and stores them with tcgen05.st.  The
+    // slot's previous scales are free once its new copies have landed (the
+    // producer refilled the slot after the MMAs that read them completed).
+    const int q = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      bool ok = true;
+      for (int kg = 0; kg < KG; ++kg, ++it) {
+        const int g = it % NG;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[g], (it / NG) & 1, abort_flag))) { ok = false; break; }
+        for (int st = 0; st < G; ++st) {
+          const int s = g * G + st;
+          const uint32_t sf_t = tmem_base + lane_base + kMx8SfCol + kMx8SfRegion * s;
+          const uint4 a = ld_shared_v4(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes) + 16 * lane);
+          const uint32_t sfb = smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbSlot) + 16 * lane;
+          const uint4 b = ld_shared_v4(sfb);
+          const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+          tmem_st_32x32b_x8(sf_t, v);
+          if (!Cfg::kStackHiLo) {
+            const uint4 c = ld_shared_v4(sfb + Cfg::kSfbBytes);
+            const uint32_t w4[4] = {c.x, c.y, c.z, c.w};
+            tmem_st_32x32b_x4(sf_t + 8, w4);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sfready[g]);
+      }
+      if (!ok) break;
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue (warps 4-7)
     const int q = warp & 3;
