@@ -1613,7 +1613,7 @@ int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const vo
   MX_CUDA(attr_err);
   const int64_t tiles = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, info.sms));
-  mxfp4_w4a4_kernel<<<grid, 256, kW4SmemBytes, s>>>(ta, tb, p);
+  mxfp4_w4a4_kernel<<<grid, kW4Threads, kW4SmemBytes, s>>>(ta, tb, p);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
 }

@@ -11,9 +11,12 @@
 // K stage).  The E8M0 scales are first rearranged (sf_block_kernel) into
 // 512-byte chunks of 128 rows x 4 scale blocks, the layout tcgen05.cp copies
 // into tensor memory: byte (r, kb) of a chunk sits at (r%32)*16 + (r/32)*4 + kb.
-// Per stage the MMA thread copies 2 SFA chunks and 4 SFB chunks into TMEM and
-// issues four K=64 MMAs; tcgen05 operations of one thread run in issue order,
-// so one TMEM scale region serves every stage.
+// Per stage four scale-writer warps (one per TMEM lane quarter) store the 2
+// SFA chunks and 4 SFB chunks from shared memory into the stage's own TMEM
+// scale region with tcgen05.st (lane i: row i of each chunk, the layout the
+// .32x128b.warpx4 copy would produce), and the MMA thread issues only the four
+// K=64 MMAs; as one tcgen05.cp per chunk from the MMA thread these copies set
+// the kernel's pace.
 #pragma once
 
 #include "common.cuh"
@@ -29,9 +32,13 @@ constexpr int kW4SfaBytes = 2 * 512;             // 2 chunks x 128 rows
 constexpr int kW4SfbBytes = 4 * 512;             // 2 row halves x 2 chunks
 constexpr int kW4StageBytes = kW4ABytes + kW4BBytes + kW4SfaBytes + kW4SfbBytes;
 constexpr int kW4OffBar = kW4Stages * kW4StageBytes;
-constexpr int kW4SmemBytes = kW4OffBar + (2 * kW4Stages + 3) * 8 + 64 + 1024;
-constexpr uint32_t kW4TmemCols = 512;            // accumulator 0..255, scale factors from 256
-constexpr uint32_t kW4SfaCol = 256, kW4SfbCol = 264;
+constexpr int kW4SmemBytes = kW4OffBar + (3 * kW4Stages + 3) * 8 + 64 + 1024;
+constexpr int kW4Threads = 384;                  // warps 0-1 copies / MMA, 4-7 epilogue, 8-11 scale writers
+constexpr uint32_t kW4TmemCols = 512;            // accumulator 0..255, scale regions from 256
+// scale region of stage slot s at column 256 + 24 s: SFA chunks c = 0, 1 at
+// +4c, SFB chunk (c, row half h) at +8 + 8c + 4h
+constexpr uint32_t kW4SfCol = 256, kW4SfRegion = 24;
+static_assert(kW4SfCol + kW4Stages * kW4SfRegion <= kW4TmemCols, "W4A4 scale regions in tensor memory");
 
 struct W4A4Params {
   int M, N, K;
@@ -92,7 +99,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kW4Threads, 1)
     mxfp4_w4a4_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const W4A4Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -102,7 +109,8 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* tfull = empty + kW4Stages;
   uint64_t* tempty = tfull + 1;
   uint64_t* drain = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sfready = drain + 1;  // [kW4Stages]: a stage's scales are in TMEM (4 scale-writer warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sfready + kW4Stages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KT = (p.K + kW4KStage - 1) / kW4KStage;
@@ -116,6 +124,7 @@ __global__ void __launch_bounds__(256, 1)
     mbar_init(tfull, 1);
     mbar_init(tempty, 4);
     mbar_init(drain, 1);
+    for (int s = 0; s < kW4Stages; ++s) mbar_init(&sfready[s], 4);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -183,23 +192,18 @@ __global__ void __launch_bounds__(256, 1)
           const int s = it % kW4Stages;
           const uint32_t ph = (it / kW4Stages) & 1;
           if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&sfready[s], ph, abort_flag)) { ok = false; break; }  // the stage's scales in TMEM
           tc_fence_after();
           uint8_t* st = smem + s * kW4StageBytes;
-          const uint32_t sfa = smem_u32(st + kW4ABytes + kW4BBytes);
-          const uint32_t sfb = sfa + kW4SfaBytes;
           const int nch = (2 * kt + 2 <= kchunks) ? 2 : kchunks - 2 * kt;
-          for (int c = 0; c < nch; ++c) {
-            tmem_cp_32x128b_warpx4(tmem_base + kW4SfaCol + 4 * c, desc_sf_chunk(sfa + c * 512));
-            tmem_cp_32x128b_warpx4(tmem_base + kW4SfbCol + 8 * c, desc_sf_chunk(sfb + c * 512));
-            tmem_cp_32x128b_warpx4(tmem_base + kW4SfbCol + 8 * c + 4, desc_sf_chunk(sfb + 1024 + c * 512));
-          }
+          const uint32_t sf_t = tmem_base + kW4SfCol + kW4SfRegion * s;
           const uint64_t adesc = desc_sw128(smem_u32(st));
           const uint64_t bdesc = desc_sw128(smem_u32(st + kW4ABytes));
           for (int j = 0; j < 2 * nch; ++j) {
             const uint32_t sf_id = (j & 1) * 2;
             const uint32_t c = j >> 1;
-            const uint32_t sfa_t = (tmem_base + kW4SfaCol + 4 * c) | (sf_id << 30);
-            const uint32_t sfb_t = (tmem_base + kW4SfbCol + 8 * c) | (sf_id << 30);
+            const uint32_t sfa_t = (sf_t + 4 * c) | (sf_id << 30);
+            const uint32_t sfb_t = (sf_t + 8 + 8 * c) | (sf_id << 30);
             const uint32_t idesc = idesc0 | (sf_id << 29) | (sf_id << 4);
             umma_mxf4(tmem_base, adesc + 2 * j, bdesc + 2 * j, idesc, sfa_t, sfb_t, (kt | j) != 0);
           }
@@ -217,6 +221,40 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
     __syncwarp();
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------------ scale writers (warps 8-11)
+    // warp 8 + q stores lane quarter q of each stage's scale region: lane i
+    // takes row i (16 bytes) of every scale chunk of the stage.  A slot's
+    // region is free again once its next copies have landed: the producer
+    // refills the slot only after the MMAs that read it completed.
+    const int q = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const int s = it % kW4Stages;
+        const uint32_t ph = (it / kW4Stages) & 1;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph, abort_flag))) { ok = false; break; }
+        const uint32_t sfa = smem_u32(smem + s * kW4StageBytes + kW4ABytes + kW4BBytes) + 16 * lane;
+        const uint32_t sfb = sfa + kW4SfaBytes;
+        // chunks past K (a last stage of 128 K) hold stale bytes in columns no MMA reads
+        const uint4 a0 = ld_shared_v4(sfa), a1 = ld_shared_v4(sfa + 512);
+        const uint4 b00 = ld_shared_v4(sfb), b01 = ld_shared_v4(sfb + 1024);   // chunk 0, row halves 0 / 1
+        const uint4 b10 = ld_shared_v4(sfb + 512), b11 = ld_shared_v4(sfb + 1536);  // chunk 1
+        const uint32_t va[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint32_t vb0[8] = {b00.x, b00.y, b00.z, b00.w, b01.x, b01.y, b01.z, b01.w};
+        const uint32_t vb1[8] = {b10.x, b10.y, b10.z, b10.w, b11.x, b11.y, b11.z, b11.w};
+        const uint32_t sf_t = tmem_base + lane_base + kW4SfCol + kW4SfRegion * s;
+        tmem_st_32x32b_x8(sf_t, va);
+        tmem_st_32x32b_x8(sf_t + 8, vb0);
+        tmem_st_32x32b_x8(sf_t + 16, vb1);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sfready[s]);
+      }
+    }
   } else if (warp >= 4) {
     const int q = warp & 3;
     const int r_local = q * 32 + lane;

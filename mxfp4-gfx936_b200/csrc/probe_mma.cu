@@ -13,6 +13,7 @@ namespace {
 constexpr int kProbeABytes = 128 * 128;            // 128 rows x 128 B (one 128B-swizzle atom column)
 constexpr int kProbeBBytes = 256 * 128;            // 256 rows x 128 B
 constexpr int kProbeSfBytes = 3 * 512;             // SFA chunk + two SFB chunks
+constexpr uint32_t kProbeSfaCol = 256, kProbeSfbCol = 264;  // their TMEM columns, after the accumulator
 constexpr int kProbeOffBar = kProbeABytes + kProbeBBytes + kProbeSfBytes;
 constexpr int kProbeSmem = kProbeOffBar + 64 + 1024;
 constexpr int64_t kProbeWaitNs = 10000000000LL;    // 10 s: the longest allowed probe runs ~0.1 s
@@ -69,14 +70,14 @@ __global__ void __launch_bounds__(128, 1) mma_rate_kernel(int iters) {
     const uint64_t adesc = desc_sw128(smem_u32(a));
     const uint64_t bdesc = desc_sw128(smem_u32(b));
     if (KIND == MXFP4_PROBE_MXF4) {
-      tmem_cp_32x128b_warpx4(tmem + kW4SfaCol, desc_sf_chunk(smem_u32(sf)));
-      tmem_cp_32x128b_warpx4(tmem + kW4SfbCol, desc_sf_chunk(smem_u32(sf + 512)));
-      tmem_cp_32x128b_warpx4(tmem + kW4SfbCol + 4, desc_sf_chunk(smem_u32(sf + 1024)));
+      tmem_cp_32x128b_warpx4(tmem + kProbeSfaCol, desc_sf_chunk(smem_u32(sf)));
+      tmem_cp_32x128b_warpx4(tmem + kProbeSfbCol, desc_sf_chunk(smem_u32(sf + 512)));
+      tmem_cp_32x128b_warpx4(tmem + kProbeSfbCol + 4, desc_sf_chunk(smem_u32(sf + 1024)));
       const uint32_t idesc = idesc_mxf4(128, 256);
       for (int i = 0; i < iters; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          umma_mxf4(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, tmem + kW4SfaCol, tmem + kW4SfbCol, (i | j) != 0);
+          umma_mxf4(tmem, adesc + 2 * j, bdesc + 2 * j, idesc, tmem + kProbeSfaCol, tmem + kProbeSfbCol, (i | j) != 0);
     } else {
       const uint32_t idesc = idesc_f16(1, 128, 256);
       for (int i = 0; i < iters; ++i)
