@@ -513,17 +513,18 @@ Mx8Act carve_mx8_act(uint8_t*& ws, int64_t rows, int64_t k, int64_t max_chunks, 
 // mx8 operand, chunk by chunk of the routing's chunk table.
 int run_mx8_split(const void* x, int64_t ldx, int64_t k, const RtRouting& rt, const int32_t* sorted, int64_t routes,
                   int top_k, const Mx8Act& a, int sms, cudaStream_t s) {
-  const int64_t blocks = rt.cap / kRtBlock;
-  if (blocks <= 0) return MXFP4_OK;
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(sms) * 2)));
+  if (rt.max_chunks <= 0) return MXFP4_OK;
+  // a CTA per chunk (up to max_chunks; those past the routing's count exit)
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(rt.max_chunks, int64_t(sms) * 2)));
   const uint16_t* xs = static_cast<const uint16_t*>(x);
   const int mc = static_cast<int>(rt.max_chunks);
   if (sorted)
-    mx8_split_kernel<true><<<grid, kMx8SplitThreads, 0, s>>>(xs, ldx, static_cast<int>(k), rt.chunks, rt.num_chunks, mc, rt.post,
-                                                sorted, static_cast<int>(routes), top_k, a.xh, a.xl, a.sfh, a.sfl);
+    mx8_split_kernel<true><<<grid, kMx8SplitThreads, 0, s>>>(xs, ldx, static_cast<int>(k), rt.chunks, rt.num_chunks,
+                                                             mc, sorted, static_cast<int>(routes), top_k, a.xh, a.xl,
+                                                             a.sfh, a.sfl);
   else
-    mx8_split_kernel<false><<<grid, kMx8SplitThreads, 0, s>>>(xs, ldx, static_cast<int>(k), rt.chunks, rt.num_chunks, mc, rt.post,
-                                                 nullptr, 0, 1, a.xh, a.xl, a.sfh, a.sfl);
+    mx8_split_kernel<false><<<grid, kMx8SplitThreads, 0, s>>>(xs, ldx, static_cast<int>(k), rt.chunks, rt.num_chunks,
+                                                              mc, nullptr, 0, 1, a.xh, a.xl, a.sfh, a.sfl);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
 }

@@ -246,49 +246,29 @@ __device__ __forceinline__ void mx8_split_piece(uint2 raw, uint32_t& hi4, uint32
 }
 
 // Split BF16 rows into E4M3 hi/lo codes and their E8M0 scales.  CTA per
-// 32-row block of the routed layout (rows [0, *post)); its chunk (the one
-// whose rows hold the block) is found by a binary search of the chunk table.
-// Warp per row (32 warps), up to sixteen 128-value pieces loaded at a time
-// (lane l: values 4l..4l+3 of each piece).  GATHER: routed row r is
-// activation row sorted[r] / top_k (zeros for a padding entry); otherwise row
-// r of `x`.
+// route chunk of the routing's chunk table (up to 128 rows), warp per row (32
+// warps), up to sixteen 128-value pieces loaded at a time (lane l: values
+// 4l..4l+3 of each piece).  GATHER: routed row r is activation row
+// sorted[r] / top_k (zeros for a padding entry); otherwise row r of `x`.
 constexpr int kMx8SplitBatch = 16;
 constexpr int kMx8SplitThreads = 1024;
 template <bool GATHER>
 __global__ void __launch_bounds__(kMx8SplitThreads) mx8_split_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                                          const int4* __restrict__ chunks,
                                                          const int32_t* __restrict__ num_chunks, int max_chunks,
-                                                         const int32_t* __restrict__ post,
                                                          const int32_t* __restrict__ sorted, int num_routes,
                                                          int top_k, uint8_t* __restrict__ xh,
                                                          uint8_t* __restrict__ xl, uint8_t* __restrict__ sfh,
                                                          uint8_t* __restrict__ sfl) {
   // sfl == sfh + 4: lo's scales in the chunk's next 32-row column (32-route chunks)
-  __shared__ int s_chunk[2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   int nch = num_chunks[0];
   nch = nch < max_chunks ? nch : max_chunks;
-  const int nblocks = post[0] / 32;
   const int KC = K / 128;
-  for (int b = blockIdx.x; b < nblocks; b += gridDim.x) {
-    __syncthreads();  // s_chunk of the previous block is no longer read
-    if (threadIdx.x == 0) {
-      // last chunk with first row <= 32 b
-      int lo = 0, hi = nch - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (chunks[mid].x <= 32 * b) lo = mid;
-        else hi = mid - 1;
-      }
-      s_chunk[0] = lo;
-      s_chunk[1] = chunks[lo].x;
-    }
-    __syncthreads();
-    const int ci = s_chunk[0];
-    const int j0 = 32 * b - s_chunk[1];  // row of the block's first route within its chunk
-    for (int i = warp; i < 32; i += nwarps) {
-      const int64_t r = 32 * static_cast<int64_t>(b) + i;
-      const int j = j0 + i;
+  for (int ci = blockIdx.x; ci < nch; ci += gridDim.x) {
+    const int4 ch = chunks[ci];
+    for (int j = warp; j < ch.y; j += nwarps) {
+      const int64_t r = static_cast<int64_t>(ch.x) + j;
       int64_t src = r;
       if (GATHER) {
         const int sid = sorted[r];
