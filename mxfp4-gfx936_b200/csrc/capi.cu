@@ -509,8 +509,9 @@ Mx8Act carve_mx8_act(uint8_t*& ws, int64_t rows, int64_t k, int64_t max_chunks, 
   return a;
 }
 
-// Split BF16 rows (gathered in routed order when `sorted` is given) into the
-// mx8 operand, chunk by chunk of the routing's chunk table.
+// Split BF16 rows into the mx8 operand, chunk by chunk of the routing's chunk
+// table: gathered in routed order when `sorted` is given, else rows already
+// in routed order; padding rows are skipped either way.
 int run_mx8_split(const void* x, int64_t ldx, int64_t k, const RtRouting& rt, const int32_t* sorted, int64_t routes,
                   int top_k, const Mx8Act& a, int sms, cudaStream_t s) {
   if (rt.max_chunks <= 0) return MXFP4_OK;
@@ -524,7 +525,8 @@ int run_mx8_split(const void* x, int64_t ldx, int64_t k, const RtRouting& rt, co
                                                              a.sfh, a.sfl);
   else
     mx8_split_kernel<false><<<grid, kMx8SplitThreads, 0, s>>>(xs, ldx, static_cast<int>(k), rt.chunks, rt.num_chunks,
-                                                              mc, nullptr, 0, 1, a.xh, a.xl, a.sfh, a.sfl);
+                                                              mc, rt.sorted, static_cast<int>(routes), 1, a.xh, a.xl,
+                                                              a.sfh, a.sfl);
   MX_CUDA(cudaGetLastError());
   return MXFP4_OK;
 }

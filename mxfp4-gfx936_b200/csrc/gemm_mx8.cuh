@@ -249,7 +249,10 @@ __device__ __forceinline__ void mx8_split_piece(uint2 raw, uint32_t& hi4, uint32
 // route chunk of the routing's chunk table (up to 128 rows), warp per row (32
 // warps), up to sixteen 128-value pieces loaded at a time (lane l: values
 // 4l..4l+3 of each piece).  GATHER: routed row r is activation row
-// sorted[r] / top_k (zeros for a padding entry); otherwise row r of `x`.
+// sorted[r] / top_k; otherwise row r of `x`.  Padding rows (sorted[r] >=
+// num_routes) are skipped: a B row only reaches its own output column of the
+// MMA, which the epilogue drops for padding, so whatever those rows and their
+// scales hold never reaches a result.
 constexpr int kMx8SplitBatch = 16;
 constexpr int kMx8SplitThreads = 1024;
 template <bool GATHER>
@@ -269,17 +272,15 @@ __global__ void __launch_bounds__(kMx8SplitThreads) mx8_split_kernel(const uint1
     const int4 ch = chunks[ci];
     for (int j = warp; j < ch.y; j += nwarps) {
       const int64_t r = static_cast<int64_t>(ch.x) + j;
-      int64_t src = r;
-      if (GATHER) {
-        const int sid = sorted[r];
-        src = sid < num_routes ? sid / top_k : -1;
-      }
-      const uint16_t* xrow = src >= 0 ? x + src * ldx + 4 * lane : nullptr;
+      const int sid = sorted[r];
+      if (sid >= num_routes) continue;  // padding (uniform over the warp)
+      const int64_t src = GATHER ? sid / top_k : r;
+      const uint16_t* xrow = x + src * ldx + 4 * lane;
       for (int c0 = 0; c0 < KC; c0 += kMx8SplitBatch) {
         uint2 raw[kMx8SplitBatch];
 #pragma unroll
         for (int u = 0; u < kMx8SplitBatch; ++u)
-          raw[u] = (xrow && c0 + u < KC) ? *reinterpret_cast<const uint2*>(xrow + (c0 + u) * 128) : make_uint2(0u, 0u);
+          raw[u] = c0 + u < KC ? *reinterpret_cast<const uint2*>(xrow + (c0 + u) * 128) : make_uint2(0u, 0u);
 #pragma unroll
         for (int u = 0; u < kMx8SplitBatch; ++u) {
           const int c = c0 + u;
