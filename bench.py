@@ -307,7 +307,7 @@ def probe_peaks():
     return out
 
 
-DECODE_ONCE_ROW_BLOCKS = 6  # mirrors kDecodeOnceRowBlocks in csrc/capi.cu
+DECODE_ONCE_ROW_BLOCKS = 4  # mirrors kDecodeOnceRowBlocks in csrc/capi.cu
 
 
 def bench_e2e_linear(soft, shape, steps, warmup, device):
@@ -766,7 +766,7 @@ def main():
     ms = bench_linear(soft, QKV, args.steps, args.warmup, 4, "fused", device, sampler=sampler)
     flops = 2.0 * m * n * k
     tflops = flops / (ms * 1e-3) / 1e12
-    # decode-once (>= 6 row blocks): two launches per step, the decode kernel then the GEMM;
+    # decode-once (>= 4 row blocks): two launches per step, the decode kernel then the GEMM;
     # each launch is timed on its own with CUDA events around graph replays of it alone
     decode_once = (m + 255) // 256 >= DECODE_ONCE_ROW_BLOCKS
     dec_ms = bench_decode_kernel(soft, QKV, args.steps, args.warmup, device) if decode_once else 0.0

@@ -703,9 +703,12 @@ int mxfp4_dequant(const void* packed, const void* scales, void* out, int out_dty
 // Fused mode decodes inside the GEMM producer, once per 256-row block of x.
 // From this many row blocks on, decoding each weight element once (the decode
 // kernel into an L2-resident BF16 copy, then the TMA-fed pair GEMM) costs less
-// SM time than re-decoding it per row block (measured crossover on B200: 6
-// blocks at the config-1 qkv shape, 8 at o_proj).
-constexpr int64_t kDecodeOnceRowBlocks = 6;
+// time than re-decoding it per row block.  Measured on B200 at the config-1
+// qkv shape with the weights cold in HBM (32 rotating weight sets, as a layer
+// of a served model sees them): M = 1024 / 1280 (4 / 5 row blocks) 37.5 /
+// 37.7 us decode-once against 43.0 / 44.9 us in the GEMM; at 2-3 row blocks the
+// in-GEMM decode is ~4% faster.
+constexpr int64_t kDecodeOnceRowBlocks = 4;
 
 size_t mxfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int x_dtype, int mode) {
   (void)x_dtype;

@@ -154,7 +154,7 @@ def test_fused_repeatable_full_size(monkeypatch):
 
 
 def test_fused_many_row_blocks_strided_weights(monkeypatch):
-    # >= 6 row blocks with a weight view that is not contiguous: the fused mode
+    # >= 4 row blocks with a weight view that is not contiguous: the fused mode
     # cannot use its decode-once copy and decodes inside the GEMM instead
     x, w, s = _inputs(1600, 384, 512, seed=33)
     wide = torch.cat([w, w], dim=1)
