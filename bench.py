@@ -396,7 +396,7 @@ def moe_weight_bytes(tid, cfg=MOE):
 
 def moe_kernel_name(routes, experts):
     """The grouped GEMM the MoE layer (BF16) runs at this route count."""
-    if routes <= 64:
+    if routes <= 24:
         return "routed GEMV"
     if routes < 128 * experts:
         return "block-scaled routed GEMM (E2M1 x E4M3 hi/lo, " + ("32" if routes < 48 * experts else "128") + "-route tiles)"

@@ -190,13 +190,14 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
 /* scratch comes from an 8 MiB static device array of the library (held on  */
 /* every GPU that loads it until exit).  A request needing more scratch than */
 /* that (mxfp4_fused_moe_workspace_size() > 8 MiB) returns                   */
-/* MXFP4_ERR_WORKSPACE.  Up to 64 routes (the routed GEMV) the scratch is   */
-/* only A converted to the operand dtype, none for BF16 A and C; above that */
-/* it holds the routing and A in routed order (BF16 C: split into two E4M3  */
-/* parts with their scales), every expert padded to 32 rows.  With BF16 A   */
-/* and C, 128 experts and top-8 it takes up to 8 tokens at K = 2048 and 112 */
-/* at K = 768 (decode-sized calls); bigger calls go to mxfp4_fused_moe with */
-/* a workspace.  Bad                                                        */
+/* MXFP4_ERR_WORKSPACE.  While the routed GEMV runs (up to 24 routes with  */
+/* BF16 C, 64 otherwise) the scratch is only A converted to the operand     */
+/* dtype, none for BF16 A and C; above that it holds the routing and A in   */
+/* routed order (BF16 C: split into two E4M3 parts with their scales),      */
+/* every expert padded to 32 rows.  With BF16 A and C, 128 experts and      */
+/* top-8 it takes up to 7 tokens at K = 2048 and 112 at K = 768             */
+/* (decode-sized calls); bigger calls go to mxfp4_fused_moe with a          */
+/* workspace.  Bad                                                          */
 /* sizes or dtypes return MXFP4_ERR_INVALID_ARGUMENT before any sizing.      */
 /* The first call on a device looks up the array's                          */
 /* device address, so make it before any stream capture.  All calls share    */

@@ -1203,12 +1203,18 @@ constexpr int64_t kPairRoutesPerExpert = 128;
 bool moe_pair_path(int64_t routes, int num_experts) {
   return routes >= kPairRoutesPerExpert * static_cast<int64_t>(num_experts);
 }
-// Up to kMoeGemvMaxRoutes routes (decode batches) the routed GEMV
-// (gemv_routed.cuh) runs instead: no routing pass, no routed copy, each
-// expert's weights read straight from HBM by the routes that use them.  The
-// op's FP32-precision mode with F16/F32 activations (split BF16 parts) keeps
-// the grouped GEMMs.
-bool moe_gemv_path(int64_t routes, const MoeCompute& mc) { return routes <= kMoeGemvMaxRoutes && mc.parts == 1; }
+// For decode batches the routed GEMV (gemv_routed.cuh) runs instead: no
+// routing pass, no routed copy, each expert's weights read straight from HBM
+// by the routes that use them.  Calls that can take the block-scaled grouped
+// GEMM (`mx8`, below) use it up to kMoeGemvRoutesMx8 routes, the others up to
+// kMoeGemvMaxRoutes (measured at the config-2 layer shape: T = 2 / 4 / 8 at
+// top-8 take 38 / 67 / 123 us on the GEMV, 51 / 61 / 77 us on the block-scaled
+// GEMM).  The op's FP32-precision mode with F16/F32 activations (split BF16
+// parts) keeps the grouped GEMMs.
+constexpr int64_t kMoeGemvRoutesMx8 = 24;
+bool moe_gemv_path(int64_t routes, const MoeCompute& mc, bool mx8) {
+  return routes <= (mx8 ? kMoeGemvRoutesMx8 : kMoeGemvMaxRoutes) && mc.parts == 1;
+}
 // Above that and below kPairRoutesPerExpert routes per expert, calls with a
 // BF16 result run the block-scaled grouped GEMM (gemm_mx8.cuh) when the
 // weights' alignment allows it: no weight decode.
@@ -1282,7 +1288,10 @@ size_t mxfp4_fused_moe_workspace_size(int64_t num_tokens, int top_k, int num_exp
   const int64_t cap = route_capacity(routes, num_experts, pair ? kP2BM : kRtBlock);
   const MoeCompute mc = moe_compute(a_dtype, c_dtype);
   const int64_t ka = k * mc.parts;  // columns of the converted activations
-  if (moe_gemv_path(routes, mc)) return a_dtype != mc.dtype ? align_up(static_cast<size_t>(num_tokens) * k * 2, 256) : 0;
+  // sized as if the weights allow the block-scaled kernel; if they do not, the
+  // GEMV that runs instead needs less
+  if (moe_gemv_path(routes, mc, mx8_dtypes(c_dtype)))
+    return a_dtype != mc.dtype ? align_up(static_cast<size_t>(num_tokens) * k * 2, 256) : 0;
   size_t b = pair ? pair_routing_bytes(routes, num_experts) : rt_routing_bytes(routes, num_experts);
   if (a_dtype != mc.dtype || mc.parts > 1) b += align_up(static_cast<size_t>(num_tokens) * ka * 2, 256);
   b += align_up(static_cast<size_t>(std::max<int64_t>(cap, 1)) * ka * 2, 256);  // activations in routed order
@@ -1335,7 +1344,8 @@ int mxfp4_fused_moe(const void* A, int a_dtype, const void* a_mx_scale, const vo
   MX_CUDA(cudaMemsetAsync(C, 0, static_cast<size_t>(routes) * n * esz, s));
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  if (moe_gemv_path(routes, mc)) {
+  const bool mx8 = mx8_dtypes(c_dtype) && mx8_weights_ok(B, B_mx_scale);
+  if (moe_gemv_path(routes, mc, mx8)) {
     const void* a_eff;
     if (int rc = convert_activations(A, a_dtype, a_mx_scale, mc, num_tokens, k, ws, info, s, stream, a_eff)) return rc;
     MoeGemvParams g{};
@@ -1627,7 +1637,10 @@ int mxfp4_gemm_w4a4(const void* a, const void* a_scales, const void* b, const vo
 size_t mxfp4_moe_layer_workspace_size(int64_t num_tokens, int top_k, int num_experts, int64_t hidden,
                                       int64_t inter) {
   const int64_t routes = num_tokens * top_k;
-  if (routes <= kMoeGemvMaxRoutes)  // routed GEMV: h and the weighted down rows, by route
+  // routed GEMV: h and the weighted down rows, by route (sized as if the
+  // weights allow the block-scaled kernel; the GEMV that runs instead if they
+  // do not needs less than that kernel's workspace)
+  if (routes <= kMoeGemvRoutesMx8)
     return align_up(static_cast<size_t>(routes) * inter * 2, 256) + align_up(static_cast<size_t>(routes) * hidden * 2, 256);
   const bool pair = moe_pair_path(routes, num_experts);
   const int64_t cap = std::max<int64_t>(route_capacity(routes, num_experts, pair ? kP2BM : kRtBlock), 1);
@@ -1672,7 +1685,8 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
   if (num_tokens == 0) return MXFP4_OK;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   void* ybuf = nullptr;  // [routes, hidden]: the weighted down rows, by route id
-  if (routes <= kMoeGemvMaxRoutes) {
+  const bool mx8 = mx8_weights_ok(w13, w13_scale) && mx8_weights_ok(w2, w2_scale);
+  if (routes <= (mx8 ? kMoeGemvRoutesMx8 : kMoeGemvMaxRoutes)) {
     // few routes: routed GEMVs straight from the token rows, h by route
     void* hbuf = ws;
     ws += align_up(static_cast<size_t>(routes) * inter * 2, 256);
@@ -1719,7 +1733,7 @@ int mxfp4_moe_layer(const void* x, const void* w13, const void* w13_scale, const
     d.w_dtype = w_dtype;
     d.mul_w = 1;
     if (int rc = launch_moe_gemv<EPI_MOE, false>(d, s)) return rc;
-  } else if (!moe_pair_path(routes, num_experts) && mx8_weights_ok(w13, w13_scale) && mx8_weights_ok(w2, w2_scale)) {
+  } else if (!moe_pair_path(routes, num_experts) && mx8) {
     // block-scaled grouped GEMMs: x and h split into E4M3 hi/lo in routed order
     const int bn = mx8_bn(routes, num_experts);
     const RtRouting rt = carve_rt_routing(ws, routes, num_experts, bn);

@@ -31,7 +31,7 @@
 
 namespace mx {
 
-constexpr int kMoeGemvMaxRoutes = 64;  // routes per call up to which the routed calls use this kernel
+constexpr int kMoeGemvMaxRoutes = 64;  // routes per call up to which the routed calls may use this kernel
 constexpr int kMoeGemvWarps = 8;       // outputs (rows) per CTA
 
 struct MoeGemvParams {
