@@ -341,6 +341,15 @@ int run_route(const void* ids, int ids_dtype, int64_t num_routes, int num_expert
               int32_t* post, int64_t capacity, uint8_t* ws, cudaStream_t stream,
               int4* rt_chunks = nullptr, int32_t* rt_num_chunks = nullptr, int chunk_blocks = kRtChunkBlocks) {
   RouteWs r = carve_route_ws(ws, num_routes, num_experts);
+  if (num_routes <= kRouteSmallMax && num_experts <= kRouteSmallExperts) {
+    // decode-sized calls: the whole routing in one CTA (one launch instead of three)
+    const size_t smem_small = sizeof(int32_t) * 32 * num_experts;
+    route_small_kernel<<<1, 1024, smem_small, stream>>>(ids, ids_dtype, num_routes, num_experts, expert_offset,
+                                                        block_m, r.blk_off, sorted_ids, block_expert, post,
+                                                        capacity / block_m, rt_chunks, rt_num_chunks, chunk_blocks);
+    MX_CUDA(cudaGetLastError());
+    return MXFP4_OK;
+  }
   const int64_t chunks = std::max<int64_t>((num_routes + kRouteThreads - 1) / kRouteThreads, 1);
   const size_t smem = sizeof(int32_t) * kRouteWarps * num_experts;
   static std::once_flag once;

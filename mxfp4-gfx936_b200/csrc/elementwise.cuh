@@ -178,6 +178,79 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
 
 constexpr int kOffsetsTileInts = 9216;  // 36 KB of counts per tile
 
+// The routed layout from the per-expert route counts total_s[] (shared
+// memory; one CTA of 1024 threads, every thread calls this): blk_off[e] and
+// scan_s[e] = first block of expert e, the per-block expert ids, the pad
+// entries of every expert's last block, the used length and, with rt_chunks,
+// the chunk table.  Ends with scan_s valid for every thread.
+__device__ __forceinline__ void route_layout(const int32_t* total_s, int32_t* scan_s, int32_t* warp_sums,
+                                             int num_experts, int block_m, int64_t num_routes,
+                                             int32_t* __restrict__ blk_off, int32_t* __restrict__ sorted_ids,
+                                             int32_t* __restrict__ block_expert,
+                                             int32_t* __restrict__ num_post_padded, int64_t capacity_blocks,
+                                             int4* __restrict__ rt_chunks, int32_t* __restrict__ rt_num_chunks,
+                                             int chunk_blocks) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  // exclusive scan of padded block counts over experts (E <= 1024: one per thread)
+  const int e = threadIdx.x;
+  const int nb = e < num_experts ? (total_s[e] + block_m - 1) / block_m : 0;
+  int blocks_total;
+  const int excl_in_warp = warp_excl_scan(nb, lane, blocks_total);
+  if (lane == 0) warp_sums[wid] = blocks_total;
+  __syncthreads();
+  if (wid == 0) {
+    int t;
+    const int ex = warp_excl_scan(warp_sums[lane], lane, t);
+    warp_sums[lane] = ex;  // exclusive over warps
+    if (lane == 0) num_post_padded[0] = t * block_m;
+  }
+  __syncthreads();
+  const int excl = excl_in_warp + warp_sums[wid];
+  if (e < num_experts) {
+    scan_s[e] = excl;
+    blk_off[e] = excl;
+  }
+  __syncthreads();
+  const int used_blocks = num_experts > 0 ? scan_s[num_experts - 1] +
+                                                (total_s[num_experts - 1] + block_m - 1) / block_m
+                                          : 0;
+  for (int64_t b = used_blocks + threadIdx.x; b < capacity_blocks; b += blockDim.x) block_expert[b] = -1;
+  // per-block expert ids and the pad entries of every expert's last block: warp per expert
+  const int32_t pad = static_cast<int32_t>(num_routes);
+  for (int x = wid; x < num_experts; x += 32) {
+    const int cnt = total_s[x];
+    const int nbx = (cnt + block_m - 1) / block_m;
+    const int first = scan_s[x];
+    for (int b = lane; b < nbx; b += 32) block_expert[first + b] = x;
+    const int64_t base = static_cast<int64_t>(first) * block_m;
+    for (int i = cnt + lane; i < nbx * block_m; i += 32) sorted_ids[base + i] = pad;
+  }
+  __syncthreads();
+  if (rt_chunks == nullptr) return;  // uniform: every thread returns (scan_s is complete)
+  // chunk table: exclusive scan of the per-expert chunk counts (one expert per thread)
+  const int nc = e < num_experts ? (nb + chunk_blocks - 1) / chunk_blocks : 0;
+  int chunks_total;
+  const int cexcl_in_warp = warp_excl_scan(nc, lane, chunks_total);
+  if (lane == 0) warp_sums[wid] = chunks_total;
+  __syncthreads();
+  if (wid == 0) {
+    int t;
+    const int ex = warp_excl_scan(warp_sums[lane], lane, t);
+    warp_sums[lane] = ex;
+    if (lane == 0) rt_num_chunks[0] = t;
+  }
+  __syncthreads();
+  if (e < num_experts) {
+    const int c0 = cexcl_in_warp + warp_sums[wid];
+    for (int i = 0; i < nc; ++i) {
+      const int b0 = i * chunk_blocks;
+      const int nbl = min(chunk_blocks, nb - b0);
+      rt_chunks[c0 + i] = make_int4((excl + b0) * block_m, nbl * block_m, e, 0);
+    }
+  }
+  __syncthreads();
+}
+
 // Optional route chunks for the routed GEMMs (rt_chunks != nullptr): every
 // expert's padded rows are cut into chunks of at most chunk_blocks blocks;
 // chunk i of the table is int4 {first row, rows, expert, 0}, in expert order,
@@ -222,63 +295,8 @@ __global__ void __launch_bounds__(1024) route_offsets_kernel(
     __syncthreads();
   }
   __syncthreads();
-  // exclusive scan of padded block counts over experts (E <= 1024: one per thread)
-  const int e = threadIdx.x;
-  const int nb = e < num_experts ? (total_s[e] + block_m - 1) / block_m : 0;
-  int blocks_total;
-  const int excl_in_warp = warp_excl_scan(nb, lane, blocks_total);
-  if (lane == 0) warp_sums[wid] = blocks_total;
-  __syncthreads();
-  if (wid == 0) {
-    int t;
-    const int ex = warp_excl_scan(warp_sums[lane], lane, t);
-    warp_sums[lane] = ex;  // exclusive over warps
-    if (lane == 0) num_post_padded[0] = t * block_m;
-  }
-  __syncthreads();
-  const int excl = excl_in_warp + warp_sums[wid];
-  if (e < num_experts) {
-    scan_s[e] = excl;
-    blk_off[e] = excl;
-  }
-  __syncthreads();
-  const int used_blocks = num_experts > 0 ? scan_s[num_experts - 1] +
-                                                (total_s[num_experts - 1] + block_m - 1) / block_m
-                                          : 0;
-  for (int64_t b = used_blocks + threadIdx.x; b < capacity_blocks; b += blockDim.x) block_expert[b] = -1;
-  // per-block expert ids and the pad entries of every expert's last block: warp per expert
-  const int32_t pad = static_cast<int32_t>(num_routes);
-  for (int x = wid; x < num_experts; x += 32) {
-    const int cnt = total_s[x];
-    const int nbx = (cnt + block_m - 1) / block_m;
-    const int first = scan_s[x];
-    for (int b = lane; b < nbx; b += 32) block_expert[first + b] = x;
-    const int64_t base = static_cast<int64_t>(first) * block_m;
-    for (int i = cnt + lane; i < nbx * block_m; i += 32) sorted_ids[base + i] = pad;
-  }
-  if (rt_chunks == nullptr) return;
-  // chunk table: exclusive scan of the per-expert chunk counts (one expert per thread)
-  __syncthreads();
-  const int nc = e < num_experts ? (nb + chunk_blocks - 1) / chunk_blocks : 0;
-  int chunks_total;
-  const int cexcl_in_warp = warp_excl_scan(nc, lane, chunks_total);
-  if (lane == 0) warp_sums[wid] = chunks_total;
-  __syncthreads();
-  if (wid == 0) {
-    int t;
-    const int ex = warp_excl_scan(warp_sums[lane], lane, t);
-    warp_sums[lane] = ex;
-    if (lane == 0) rt_num_chunks[0] = t;
-  }
-  __syncthreads();
-  if (e < num_experts) {
-    const int c0 = cexcl_in_warp + warp_sums[wid];
-    for (int i = 0; i < nc; ++i) {
-      const int b0 = i * chunk_blocks;
-      const int nbl = min(chunk_blocks, nb - b0);
-      rt_chunks[c0 + i] = make_int4((excl + b0) * block_m, nbl * block_m, e, 0);
-    }
-  }
+  route_layout(total_s, scan_s, warp_sums, num_experts, block_m, num_routes, blk_off, sorted_ids, block_expert,
+               num_post_padded, capacity_blocks, rt_chunks, rt_num_chunks, chunk_blocks);
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_scatter_kernel(
@@ -293,6 +311,51 @@ __global__ void __launch_bounds__(kRouteThreads) route_scatter_kernel(
   const int64_t pos = static_cast<int64_t>(blk_off[e]) * block_m +
                       hist[static_cast<int64_t>(blockIdx.x) * num_experts + e] + rk;
   sorted_ids[pos] = static_cast<int32_t>(r);
+}
+
+// Routing of up to kRouteSmallMax routes over up to kRouteSmallExperts experts
+// in one CTA of 1024 threads (decode-sized calls): the stable ranks of
+// route_count_kernel (a route per thread; __match_any_sync within the warp,
+// exclusive prefix over the warps per expert), then route_layout, then the
+// scatter of route_scatter_kernel.  Same metadata as the three-kernel path.
+constexpr int kRouteSmallMax = 1024;
+constexpr int kRouteSmallExperts = 256;
+__global__ void __launch_bounds__(1024) route_small_kernel(
+    const void* __restrict__ ids, int ids_dtype, int64_t num_routes, int num_experts, int expert_offset,
+    int block_m, int32_t* __restrict__ blk_off, int32_t* __restrict__ sorted_ids,
+    int32_t* __restrict__ block_expert, int32_t* __restrict__ num_post_padded, int64_t capacity_blocks,
+    int4* __restrict__ rt_chunks, int32_t* __restrict__ rt_num_chunks, int chunk_blocks) {
+  extern __shared__ int32_t warp_cnt[];  // [32][num_experts]
+  __shared__ int32_t total_s[kMaxExperts];
+  __shared__ int32_t scan_s[kMaxExperts];
+  __shared__ int32_t warp_sums[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 32 * num_experts; i += blockDim.x) warp_cnt[i] = 0;
+  __syncthreads();
+  const int r = threadIdx.x;
+  int e = -1;
+  if (r < num_routes) {
+    e = load_expert(ids, ids_dtype, r) - expert_offset;
+    if (e < 0 || e >= num_experts) e = -1;
+  }
+  const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+  const int rank_in_warp = __popc(peers & ((1u << lane) - 1u));
+  if (e >= 0 && rank_in_warp == 0) warp_cnt[warp * num_experts + e] = __popc(peers);
+  __syncthreads();
+  for (int x = threadIdx.x; x < num_experts; x += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = warp_cnt[w * num_experts + x];
+      warp_cnt[w * num_experts + x] = run;
+      run += c;
+    }
+    total_s[x] = run;
+  }
+  __syncthreads();
+  route_layout(total_s, scan_s, warp_sums, num_experts, block_m, num_routes, blk_off, sorted_ids, block_expert,
+               num_post_padded, capacity_blocks, rt_chunks, rt_num_chunks, chunk_blocks);
+  if (e >= 0)
+    sorted_ids[static_cast<int64_t>(scan_s[e]) * block_m + warp_cnt[warp * num_experts + e] + rank_in_warp] = r;
 }
 
 // ---------------------------------------------------------------------------
