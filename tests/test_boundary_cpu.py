@@ -234,3 +234,21 @@ def test_probe_library_exports_its_header():
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     assert fn(7, 10, None, None, None) == 1
+
+
+def test_noalloc_limits_stated_in_the_header_hold():
+    # include/mxfp4_b200.h states what the 8 MiB static scratch of
+    # mxfp4_fused_moe_noalloc admits with BF16 A and C, 128 experts and top-8:
+    # up to 7 tokens at K = 2048 and 112 at K = 768; the entry point compares
+    # the workspace size of the call with the array's size
+    lib = ctypes.CDLL(str(PKG / "libmxfp4_b200.so"))
+    size = lib.mxfp4_fused_moe_workspace_size
+    size.restype = ctypes.c_size_t
+    size.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                     ctypes.c_int]
+    BF16, limit = 1, 8 << 20
+    for k, n, most in [(2048, 1536, 7), (768, 2048, 112)]:
+        assert all(size(t, 8, 128, n, k, BF16, BF16) <= limit for t in range(1, most + 1))
+        assert size(most + 1, 8, 128, n, k, BF16, BF16) > limit
+    text = (ROOT / "include" / "mxfp4_b200.h").read_text()
+    assert "up to 7 tokens at K = 2048 and 112" in text

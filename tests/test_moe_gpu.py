@@ -139,6 +139,44 @@ def test_moe_layer_matches_reference_golden():
     assert ok, (err, bound, rel)
 
 
+# 16 and 100 routes per expert: the block-scaled routed GEMM with 32- and
+# 128-route tiles
+@pytest.mark.parametrize("m,top_k,e", [(64, 4, 16), (200, 4, 8)])
+def test_moe_op_block_scaled_wide_range_activations(m, top_k, e):
+    # BF16 activations whose 32-value blocks sit anywhere from 2^-30 to 2^30 and
+    # span up to 2^24 inside a block, with all-zero blocks, signed zeros and
+    # all-zero tokens: the block-scaled GEMM writes every activation as two E4M3
+    # parts under per-block scales, which must stay within the tolerance of the
+    # oracle's exact products on every route's row, not just overall
+    n, k = 256, 512
+    g = torch.Generator().manual_seed(91)
+    mant = torch.randn(m, k, generator=g)
+    block_exp = torch.randint(-30, 31, (m, k // 32, 1), generator=g).float().expand(m, k // 32, 32).reshape(m, k)
+    spread = torch.randint(-24, 1, (m, k), generator=g).float()
+    a = (mant * torch.exp2(block_exp + spread)).to(torch.bfloat16)
+    a[::5, :32] = 0.0
+    a[1::7, 32:64] = -0.0
+    a[3] = 0.0
+    b = torch.randint(0, 256, (e, n, k // 2), generator=g, dtype=torch.uint8)
+    bmx = torch.randint(116, 130, (e, n, k // 32), generator=g, dtype=torch.uint8)
+    ids = torch.stack([torch.randperm(e, generator=g)[:top_k] for _ in range(m)]).to(torch.int32)
+    tw = torch.rand(m, top_k, generator=g)
+    a_scale = torch.tensor([1.0])
+    b_scale = torch.ones(e)
+    c = torch.empty((m, top_k, n), dtype=torch.bfloat16, device="cuda")
+    soft.fused_moe_mxfp4_soft(a.cuda(), b.cuda(), c, a_scale.cuda(), b_scale.cuda(), None, bmx.cuda(), tw.cuda(),
+                              ids.cuda(), torch.empty(0), torch.empty(0), torch.empty(0), True, top_k, False, False)
+    ref = O.moe_op(_np(a), "fp32", None, b.numpy(), bmx.numpy(), a_scale.numpy(), b_scale.numpy(), tw.numpy(),
+                   ids.numpy(), True, "bf16")
+    got = _np(c)
+    assert np.isfinite(got).all()
+    assert (got[3] == 0).all()
+    for t in range(m):
+        for j in range(top_k):
+            ok, err, bound, rel = O.check_close(got[t, j], ref[t, j])
+            assert ok, (t, j, err, bound, rel)
+
+
 # routes per call: 2 (routed GEMV), 800 and 4104 (routed tensor-memory GEMM), 4096 over 16 experts (256 per
 # expert: the CTA-pair GEMM)
 @pytest.mark.parametrize("t,h,e,k,inter", [(1, 256, 8, 2, 128), (200, 512, 16, 4, 256), (513, 256, 64, 8, 384),
