@@ -633,6 +633,7 @@ __global__ void __launch_bounds__(Mx8Cfg<BN>::kThreads, 1)
         for (int i = etid; i < n * 8; i += 128) {
           const int j = i >> 3, c = i & 7;
           if (c * 8 >= ncols) continue;
+          if (route_ids[j] >= p.num_routes) continue;  // padding: the h split and the down GEMM drop its row
           const uint32_t row = smem_u32(stage) + j * 256;
           const uint4 h8 = rt_glu8(ld_shared_v4(row + c * 16), ld_shared_v4(row + 128 + c * 16));
           uint8_t* dst = static_cast<uint8_t*>(p.out) + ((static_cast<int64_t>(ch.x) + j) * p.ldo + col0 + c * 8) * 2;
