@@ -39,7 +39,9 @@
 // multiple of 32, at most BN).  K stages of 128:
 //   warp 0   TMA producer: per group of stages one copy each of the weight
 //            tile (unpacked E2M1), the hi and lo route tiles and the chunk's
-//            hi and lo activation scales
+//            hi and lo activation scales; the scales complete on their own
+//            barrier (with the weight scales), so the scale writers start
+//            while the tiles are still in flight
 //   warp 2   weight-scale producer: the weights' scale words (one 32-bit word
 //            = 4 codes per row and stage) by 4-byte cp.async into the
 //            512-byte chunk layout
@@ -91,7 +93,7 @@ struct Mx8Cfg {
   static constexpr int kOffRoute = kOffOut + kOutBytes;       // BN route ids + BN route weights
   static constexpr int kOffVote = kOffRoute + BN * 8;
   static constexpr int kOffBar = kOffVote + 16;
-  static constexpr int kNumBars = 3 * kSlots + 5;
+  static constexpr int kNumBars = 4 * kSlots + 5;
   static constexpr int kThreads = 384;  // warps 0-3 copies / MMA, 4-7 epilogue, 8-11 scale writers
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;
@@ -364,6 +366,7 @@ __global__ void __launch_bounds__(Mx8Cfg<BN>::kThreads, 1)
   uint64_t* tempty = tfull + 2;    // [2]
   uint64_t* drain = tempty + 2;
   uint64_t* sfready = drain + 1;   // [S]: a group's scales are in tensor memory (4 scale-writer warps)
+  uint64_t* sffull = sfready + S;  // [S]: a group's weight and activation scales landed in shared memory
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
   int32_t* route_ids = reinterpret_cast<int32_t*>(smem + Cfg::kOffRoute);
@@ -387,7 +390,8 @@ __global__ void __launch_bounds__(Mx8Cfg<BN>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int g = 0; g < S; ++g) {
-      mbar_init(&full[g], 1 + 32);  // the TMA producer's expect_tx + the scale warp's 32 cp.async arrivals
+      mbar_init(&full[g], 1);         // the TMA producer's expect_tx (weight and route tiles)
+      mbar_init(&sffull[g], 1 + 32);  // its expect_tx (activation scales) + the scale warp's 32 cp.async arrivals
       mbar_init(&empty[g], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -430,38 +434,48 @@ __global__ void __launch_bounds__(Mx8Cfg<BN>::kThreads, 1)
         bool v;
         const int row0 = static_cast<int>(mx8_weight_row<EPI>(p, ch.z, wb, 0, v));
         const int nbox = ch.y / 32;  // one box when G > 1 (BN = 32)
-        const uint32_t tx = G * (128 * 64 + 2 * ch.y * 128 + Cfg::kSfbSlot);
+        const uint32_t tx = G * (128 * 64 + 2 * ch.y * 128);
+        const uint32_t tx_sf = G * Cfg::kSfbSlot;
         for (int kg = 0; kg < KG; ++kg, ++it) {
           const int g = it % NG;
           const uint32_t ph = (it / NG) & 1;
           if (!mbar_wait(&empty[g], ph ^ 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[g], tx);
+          mbar_arrive_expect_tx(&sffull[g], tx_sf);
           armed |= 1u << g;
           armed_par = (armed_par & ~(1u << g)) | (ph << g);
           const int s0 = g * G, kt0 = kg * G;
+          // the small scale copies first: the scale writers start on them while the tiles are in flight
+          const int64_t sfo = (static_cast<int64_t>(ci) * KT + kt0) * 512;
+          if (Cfg::kStackHiLo) {
+            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot, p.sfh + sfo, G * Cfg::kSfbBytes, &sffull[g]);
+          } else {
+            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot, p.sfh + sfo, Cfg::kSfbBytes, &sffull[g]);
+            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot + Cfg::kSfbBytes, p.sfl + sfo, Cfg::kSfbBytes,
+                      &sffull[g]);
+          }
           if (EPI == EPI_GLU)
             tma_load_4d_hint(smem + Cfg::kOffA + s0 * Cfg::kABytes, &tmap_w, &full[g], 0, row0, 0, kt0, pol_w);
           else
             tma_load_3d_hint(smem + Cfg::kOffA + s0 * Cfg::kABytes, &tmap_w, &full[g], 0, row0, kt0, pol_w);
           uint8_t* bslot = smem + Cfg::kOffB + s0 * 2 * Cfg::kBBytes;
-          const int64_t sfo = (static_cast<int64_t>(ci) * KT + kt0) * 512;
           if (Cfg::kStackHiLo) {
             // [stage][hi 32 rows, lo 32 rows] in one copy; the scales of both in one chunk per stage
             tma_load_4d(bslot, &tmap_xh, &full[g], 0, ch.x, 0, kt0);
-            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot, p.sfh + sfo, G * Cfg::kSfbBytes, &full[g]);
           } else {
             for (int i = 0; i < nbox; ++i) {
               tma_load_3d(bslot + i * 32 * 128, &tmap_xh, &full[g], 0, ch.x + 32 * i, kt0);
               tma_load_3d(bslot + Cfg::kBBytes + i * 32 * 128, &tmap_xl, &full[g], 0, ch.x + 32 * i, kt0);
             }
-            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot, p.sfh + sfo, Cfg::kSfbBytes, &full[g]);
-            bulk_load(smem + Cfg::kOffSfb + s0 * Cfg::kSfbSlot + Cfg::kSfbBytes, p.sfl + sfo, Cfg::kSfbBytes, &full[g]);
           }
         }
       }
       if (!ok || *abort_flag)
         for (int g = 0; g < NG; ++g)
-          if (armed & (1u << g)) mbar_drain(&full[g], (armed_par >> g) & 1u);
+          if (armed & (1u << g)) {
+            mbar_drain(&full[g], (armed_par >> g) & 1u);
+            mbar_drain(&sffull[g], (armed_par >> g) & 1u);
+          }
     }
     __syncwarp();
   } else if (warp == 2) {
@@ -495,7 +509,7 @@ __global__ void __launch_bounds__(Mx8Cfg<BN>::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 4; ++j) cp_async_4(sfa + st * Cfg::kSfaBytes + 128 * j, srow[j] + 4 * kt);
         }
-        cp_async_arrive_noinc(&full[g]);
+        cp_async_arrive_noinc(&sffull[g]);
       }
     }
     cp_async_wait_all();
@@ -560,8 +574,9 @@ __global__ void __launch_bounds__(Mx8Cfg<BN>::kThreads, 1)
     // chunk and of its activation-scale chunk(s) from shared memory (the
     // layout tcgen05.cp .32x128b.warpx4 would copy: column j = rows 32 j + i,
     // the same in all four quarters) and stores them with tcgen05.st.  The
-    // slot's previous scales are free once its new copies have landed (the
-    // producer refilled the slot after the MMAs that read them completed).
+    // slot's previous scales are free once its new scale copies have landed
+    // (the producer and the scale warp refill a slot only after the MMAs that
+    // read it completed).
     const int q = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     int it = 0;
@@ -569,7 +584,7 @@ __global__ void __launch_bounds__(Mx8Cfg<BN>::kThreads, 1)
       bool ok = true;
       for (int kg = 0; kg < KG; ++kg, ++it) {
         const int g = it % NG;
-        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[g], (it / NG) & 1, abort_flag))) { ok = false; break; }
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&sffull[g], (it / NG) & 1, abort_flag))) { ok = false; break; }
         for (int st = 0; st < G; ++st) {
           const int s = g * G + st;
           const uint32_t sf_t = tmem_base + lane_base + kMx8SfCol + kMx8SfRegion * s;
